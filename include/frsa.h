@@ -1,0 +1,113 @@
+/*
+ * frsa.h — C ABI of the B200 (sm_100a) fused 2D-RoPE scaled-dot-product
+ * attention, forward and backward.
+ *
+ * The reference (v1kstrand/triton_fused_rope_flash_attn, file "fa_rope_full .py")
+ * has no native ABI: its Python autograd wrapper launches Triton kernels
+ * directly. Each entry point below replaces one group of those launches; the
+ * host mirror (triton_fused_rope_flash_attn_b200.TritonAttention) calls them
+ * through ctypes with torch-allocated device buffers.
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers. q, k, v, o, d_o, dq, dk, dv are
+ *     contiguous [B, H, N, D] in the I/O dtype; lse and delta are contiguous
+ *     fp32 [B, H, N]; cosp/sinp are contiguous fp32 [n_pos, D/2].
+ *   - Token t uses table row t - has_cls; token 0 is not rotated when has_cls.
+ *   - scale multiplies the logits (the reference uses 1/sqrt(D)).
+ *   - lse receives max + ln(sum) of the scaled logits per query row, the
+ *     quantity the reference stores in M (fa_rope_full .py:309).
+ *   - Launches are asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream). Entry points never allocate device memory: scratch is
+ *     passed in by the caller.
+ *   - Return value 0 = launched; otherwise an FRSA_ERR_* code, nothing launched.
+ *   - Thread-safe; no global state except the device status word below.
+ */
+#ifndef FRSA_H_
+#define FRSA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FRSA_ABI_VERSION 1
+
+enum frsa_dtype {
+  FRSA_DTYPE_BF16 = 0,
+  FRSA_DTYPE_F16 = 1,
+  FRSA_DTYPE_F32 = 2
+};
+
+enum frsa_status {
+  FRSA_OK = 0,
+  FRSA_ERR_NULL_ARG = 1,        /* a required pointer is NULL */
+  FRSA_ERR_BAD_SHAPE = 2,       /* B, H, N or D out of range, or N inconsistent with n_pos/has_cls */
+  FRSA_ERR_UNSUPPORTED_D = 3,   /* D % 8 != 0 or D > 128 */
+  FRSA_ERR_UNSUPPORTED_DTYPE = 4,
+  FRSA_ERR_MISALIGNED = 5,      /* a pointer is not 16-byte aligned */
+  FRSA_ERR_LAUNCH = 6,          /* a CUDA launch or tensor-map encode failed */
+  FRSA_ERR_DEVICE_TIMEOUT = 7,  /* a kernel gave up on a bounded wait (see frsa_query_status) */
+  FRSA_ERR_NO_DEVICE = 8,       /* the current device is not sm_100 */
+  FRSA_ERR_WORKSPACE = 9        /* the backward workspace is missing or too small */
+};
+
+typedef struct frsa_attn_args {
+  /* forward inputs / outputs */
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  /* backward inputs / outputs (ignored by frsa_fwd) */
+  const void* d_o;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* delta;       /* fp32 [B, H, N] scratch: rowsum(dO * O) */
+  void* workspace;    /* fp32 scratch of frsa_bwd_workspace_bytes() bytes, or NULL when that is 0 */
+  size_t workspace_bytes;
+  /* RoPE pair tables */
+  const float* cosp;
+  const float* sinp;
+  /* shape */
+  int64_t B, H, N, D, n_pos;
+  int32_t has_cls;
+  int32_t io_dtype;       /* enum frsa_dtype; must equal compute_dtype in this ABI version */
+  int32_t compute_dtype;  /* enum frsa_dtype: BF16 or F16 */
+  float scale;
+} frsa_attn_args;
+
+/* Forward: O = softmax(R(Q) R(K)^T * scale) V and lse.
+ * Replaces the _attn_fwd launch of TritonAttention.forward
+ * (fa_rope_full .py:1036-1057; kernel fa_rope_full .py:91-315). */
+int frsa_fwd(const frsa_attn_args* args, void* stream);
+
+/* Backward: dQ, dK, dV from d_o, o, lse (and q, k, v, tables).
+ * Replaces the three launches of TritonAttention.backward
+ * (_attn_bwd_preprocess fa_rope_full .py:1076-1082, _attn_bwd_dk_dv_rope
+ * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136). */
+int frsa_bwd(const frsa_attn_args* args, void* stream);
+
+/* Bytes of fp32 workspace frsa_bwd needs for this shape (0 when the whole
+ * head fits one CTA and dQ is reduced on chip). No reference counterpart:
+ * the reference's dQ kernel (fa_rope_full .py:708-1009) recomputes instead. */
+size_t frsa_bwd_workspace_bytes(const frsa_attn_args* args);
+
+/* Message for an FRSA_ERR_* code (static storage). */
+const char* frsa_strerror(int code);
+
+/* Synchronizes the current device, returns FRSA_ERR_DEVICE_TIMEOUT if any
+ * kernel recorded a bounded-wait timeout since the last call (and clears it),
+ * FRSA_ERR_LAUNCH on a sticky CUDA error, else FRSA_OK. */
+int frsa_query_status(void);
+
+/* FRSA_ABI_VERSION of the loaded library. */
+int frsa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRSA_H_ */

@@ -1,0 +1,125 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the float64 oracle.
+
+Inputs are seeded, quantised to the compute dtype, and the oracle is evaluated
+in float64 on exactly those quantised values with the same float32 tables.
+Bar: max abs error <= 3e-2 and mean abs error <= 1e-3 on O, dQ, dK, dV (bf16;
+for N <= 5 the mean bound is twice the error of rounding the exact result to
+bf16 when that is larger);
+LSE within 1e-2 abs. The ViT-H-like case (inputs x2.0, D=80) is checked by
+relative error instead, because rounding the exact outputs to bf16 alone
+exceeds the absolute mean bound there.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attn_bwd_np, attn_fwd_np
+from tests.helpers import MAX_ABS_TOL, MEAN_ABS_TOL, err_stats, mean_tol, rel_err, seeded_inputs
+
+pytestmark = pytest.mark.gpu
+
+# (B, H, H_img, has_cls, D, amp, dtype)
+CASES = [
+    (1, 2, 1, True, 64, 1.0, torch.bfloat16),     # N=2
+    (1, 2, 1, False, 64, 1.0, torch.bfloat16),    # N=1
+    (1, 2, 2, True, 64, 1.0, torch.bfloat16),     # N=5
+    (2, 1, 3, False, 64, 1.0, torch.bfloat16),    # N=9
+    (1, 2, 5, True, 64, 1.0, torch.bfloat16),     # N=26
+    (1, 2, 7, False, 64, 1.0, torch.bfloat16),    # N=49
+    (1, 2, 7, True, 64, 1.0, torch.bfloat16),     # N=50
+    (2, 3, 11, False, 64, 1.0, torch.bfloat16),   # N=121
+    (2, 4, 14, True, 64, 1.0, torch.bfloat16),    # N=197 (ViT-S/B)
+    (2, 4, 14, True, 64, 1.0, torch.float16),     # N=197 fp16
+    (1, 3, 16, False, 64, 1.0, torch.bfloat16),   # N=256
+    (1, 3, 16, True, 64, 1.0, torch.bfloat16),    # N=257 (atomic-dQ path)
+    (1, 2, 24, False, 64, 1.0, torch.bfloat16),   # N=576 (ViT-L)
+    (1, 2, 14, True, 32, 1.0, torch.bfloat16),    # D=32
+    (1, 2, 7, True, 80, 1.0, torch.bfloat16),     # D=80, N=50
+    (1, 2, 14, True, 128, 1.0, torch.bfloat16),   # D=128
+]
+
+
+def _run(B, H, side, has_cls, D, amp, dtype, seed=0):
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, fused_rope_attention_bwd, \
+        fused_rope_attention_fwd
+    N = side * side + (1 if has_cls else 0)
+    q, k, v, do = seeded_inputs(B, H, N, D, amp, seed)
+    dev = torch.device("cuda")
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    qd, kd, vd, dod = (t.to(dev, dtype) for t in (q, k, v, do))
+    o, lse = fused_rope_attention_fwd(qd, kd, vd, cs.COSP, cs.SINP, has_cls)
+    dq, dk, dv = fused_rope_attention_bwd(qd, kd, vd, o, lse, dod, cs.COSP, cs.SINP, has_cls)
+    torch.cuda.synchronize()
+    from triton_fused_rope_flash_attn_b200 import _lib
+    assert _lib.load().frsa_query_status() == 0
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    qn, kn, vn, don = (t.to(dtype).double().numpy() for t in (q, k, v, do))
+    o_ref, lse_ref = attn_fwd_np(qn, kn, vn, cos, sin, has_cls)
+    dq_ref, dk_ref, dv_ref = attn_bwd_np(qn, kn, vn, don, cos, sin, has_cls)
+    got = {n: t.double().cpu().numpy() for n, t in (("o", o), ("lse", lse), ("dq", dq),
+                                                     ("dk", dk), ("dv", dv))}
+    ref = {"o": o_ref, "lse": lse_ref, "dq": dq_ref, "dk": dk_ref, "dv": dv_ref}
+    return got, ref
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"B{c[0]}H{c[1]}s{c[2]}c{int(c[3])}D{c[4]}"
+                         f"{'bf16' if c[6] == torch.bfloat16 else 'f16'}")
+def test_fwd_bwd_parity(case):
+    got, ref = _run(*case)
+    for name in ("o", "dq", "dk", "dv"):
+        assert np.isfinite(got[name]).all(), name
+        mx, mean = err_stats(got[name], ref[name])
+        assert mx <= MAX_ABS_TOL, f"{name}: max abs err {mx:.3e}"
+        assert mean <= mean_tol(ref[name], case[6]), f"{name}: mean abs err {mean:.3e}"
+    mx, _ = err_stats(got["lse"], ref["lse"])
+    assert mx <= 1e-2, f"lse max abs err {mx:.3e}"
+
+
+def test_vit_h_like_relative():
+    """N=1370, D=80, inputs x2.0: relative mean error <= 1e-2 on every tensor."""
+    got, ref = _run(1, 2, 37, True, 80, 2.0, torch.bfloat16)
+    for name in ("o", "dq", "dk", "dv"):
+        assert np.isfinite(got[name]).all(), name
+        assert rel_err(got[name], ref[name]) <= 1e-2, name
+
+
+def test_autograd_wrapper_matches_direct_calls():
+    """TritonAttention.apply under bf16 autocast with fp32 leaves (README usage)."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, sdpa_triton_fa_rope
+    B, H, side, D = 2, 2, 14, 64
+    N = side * side + 1
+    q, k, v, do = seeded_inputs(B, H, N, D)
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        o = sdpa_triton_fa_rope(qd, kd, vd, cs)
+    assert o.dtype == torch.float32
+    o.backward(do.cuda())
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    qn, kn, vn = (t.bfloat16().double().numpy() for t in (q, k, v))
+    o_ref, _ = attn_fwd_np(qn, kn, vn, cos, sin, True)
+    dq_ref, dk_ref, dv_ref = attn_bwd_np(qn, kn, vn, do.bfloat16().double().numpy(), cos, sin,
+                                         True)
+    for got, r in ((o, o_ref), (qd.grad, dq_ref), (kd.grad, dk_ref), (vd.grad, dv_ref)):
+        assert got.dtype == torch.float32
+        mx, mean = err_stats(got.detach().double().cpu().numpy(), r)
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
+
+
+def test_deterministic_resident_path():
+    """N <= 256 reduces dQ on chip: two runs are bitwise identical."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, fused_rope_attention_bwd, \
+        fused_rope_attention_fwd
+    B, H, side, D = 2, 3, 14, 64
+    N = side * side + 1
+    q, k, v, do = (t.cuda().bfloat16() for t in seeded_inputs(B, H, N, D, seed=7))
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    outs = []
+    for _ in range(2):
+        o, lse = fused_rope_attention_fwd(q, k, v, cs.COSP, cs.SINP, True)
+        outs.append((o, lse) + fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP,
+                                                        True))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)

@@ -1,0 +1,162 @@
+"""Autograd wrapper and public entry of the fused 2D-RoPE attention.
+
+Mirrors ``TritonAttention`` / ``sdpa_triton_fa_rope`` of the reference
+(fa_rope_full .py:1011-1170): the same assertions and messages, the same
+output-dtype rule (outputs and gradients in the input dtype, compute in the
+autocast dtype when CUDA autocast is on), ``scale = 1/sqrt(D)``, no mask. The
+work is done by the C ABI (``include/frsa.h``) on torch's current stream.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DT_CODE = {torch.bfloat16: _lib.FRSA_DTYPE_BF16, torch.float16: _lib.FRSA_DTYPE_F16,
+            torch.float32: _lib.FRSA_DTYPE_F32}
+
+
+def _sdpa_comp_dtype(x: torch.Tensor) -> torch.dtype:
+    """Compute dtype: the CUDA autocast dtype when autocast is on, else ``x.dtype``.
+
+    fa_rope_full .py:65-73. The reference returns the matching Triton dtype and
+    raises ``TypeError`` for anything but float16/bfloat16/float32; this returns
+    the torch dtype and raises ``TypeError`` for the same cases.
+    """
+    dtype = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled() else x.dtype
+    if dtype in (torch.float16, torch.bfloat16, torch.float32):
+        return dtype
+    raise TypeError(f"unsupported compute dtype {dtype}")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _make_args(q, k, v, cosp, sinp, has_cls, comp, o=None, lse=None, d_o=None, dq=None, dk=None,
+               dv=None, delta=None, workspace=None):
+    B, H, N, D = q.shape
+    a = _lib.FrsaAttnArgs()
+    a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
+    a.o, a.lse = _ptr(o), _ptr(lse)
+    a.d_o, a.dq, a.dk, a.dv, a.delta = _ptr(d_o), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(delta)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    a.cosp, a.sinp = _ptr(cosp), _ptr(sinp)
+    a.B, a.H, a.N, a.D = B, H, N, D
+    a.n_pos = cosp.shape[0]
+    a.has_cls = int(bool(has_cls))
+    a.io_dtype = _DT_CODE[comp]
+    a.compute_dtype = _DT_CODE[comp]
+    a.scale = 1.0 / math.sqrt(D)
+    return a
+
+
+def _stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_tables(cosp, sinp, N, D, has_cls, device):
+    if cosp.dtype != torch.float32 or sinp.dtype != torch.float32:
+        raise TypeError("COSP/SINP must be float32")
+    if cosp.dim() != 2 or cosp.shape[1] != D // 2 or sinp.shape != cosp.shape:
+        raise ValueError(f"COSP/SINP must be [N_pos, {D // 2}], got {tuple(cosp.shape)} / "
+                         f"{tuple(sinp.shape)}")
+    if cosp.shape[0] < N - int(bool(has_cls)):
+        raise ValueError(f"RoPE table has {cosp.shape[0]} positions, sequence needs "
+                         f"{N - int(bool(has_cls))}")
+    if cosp.device != device or sinp.device != device:
+        raise ValueError("RoPE tables must be on the same device as Q")
+
+
+def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True):
+    """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]`` bf16/f16.
+
+    Returns ``(o, lse)`` with ``lse`` float32 ``[B, H, N]`` (natural log).
+    """
+    comp = q.dtype
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    cosp, sinp = cosp.contiguous(), sinp.contiguous()
+    B, H, N, D = q.shape
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse)
+    _lib.check(_lib.load().frsa_fwd(a, _stream_handle(q.device)), "frsa_fwd")
+    return o, lse
+
+
+def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = True):
+    """Backward through the C ABI. Returns ``(dq, dk, dv)`` in ``q.dtype``."""
+    comp = q.dtype
+    q, k, v, o, d_o = (t.contiguous() for t in (q, k, v, o, d_o))
+    cosp, sinp = cosp.contiguous(), sinp.contiguous()
+    B, H, N, D = q.shape
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    delta = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, d_o=d_o, dq=dq, dk=dk,
+                   dv=dv, delta=delta)
+    lib = _lib.load()
+    ws_bytes = lib.frsa_bwd_workspace_bytes(a)
+    ws = None
+    if ws_bytes:
+        ws = torch.empty(ws_bytes // 4, device=q.device, dtype=torch.float32)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = ws_bytes
+    _lib.check(lib.frsa_bwd(a, _stream_handle(q.device)), "frsa_bwd")
+    return dq, dk, dv
+
+
+class TritonAttention(torch.autograd.Function):
+    """Fused 2D-RoPE SDPA with the reference's autograd contract (fa_rope_full .py:1011-1138)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, cos_sin, H_img=14, has_cls=True):
+        BATCH_SIZE, NUM_HEADS, SEQ_LEN, HEAD_DIM = Q.size()
+        assert (HEAD_DIM % 4) == 0, "HEAD_DIM must be divisible by 4 (2D RoPE requires pairs)."
+        N_img = H_img ** 2
+        if has_cls:
+            assert SEQ_LEN == 1 + N_img, (
+                f"SEQ_LEN must be 1 + H_img*W_img when has_cls=True (got {SEQ_LEN} vs {1+N_img}).")
+        else:
+            assert SEQ_LEN == N_img, (
+                f"SEQ_LEN must equal H_img*W_img when has_cls=False (got {SEQ_LEN} vs {N_img}).")
+        comp = _sdpa_comp_dtype(Q)
+        if not Q.is_cuda:
+            raise RuntimeError("sdpa_triton_fa_rope needs CUDA tensors (there is no CPU path)")
+        if comp == torch.float32:
+            raise NotImplementedError(
+                "float32 compute (TF32 tensor cores) is not implemented; run under "
+                "torch.autocast('cuda', dtype=torch.bfloat16) or pass bf16/fp16 tensors")
+        COSP, SINP = cos_sin.tables()
+        _check_tables(COSP, SINP, SEQ_LEN, HEAD_DIM, has_cls, Q.device)
+        qc, kc, vc = (t.to(comp) for t in (Q, K, V))
+        o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls)
+        ctx.comp = comp
+        ctx.has_cls = has_cls
+        ctx.io_dtypes = (Q.dtype, K.dtype, V.dtype)
+        ctx.save_for_backward(qc, kc, vc, o, lse, COSP, SINP)
+        return o.to(Q.dtype)
+
+    @staticmethod
+    def backward(ctx, dO):
+        qc, kc, vc, o, lse, COSP, SINP = ctx.saved_tensors
+        dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
+                                              ctx.has_cls)
+        qd, kd, vd = ctx.io_dtypes
+        return dq.to(qd), dk.to(kd), dv.to(vd), None, None, None
+
+
+def sdpa_triton_fa_rope(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, cos_sin, *,
+                        has_cls: bool = True, H_img: int | None = None):
+    """Fused 2D-RoPE SDPA forward; differentiable (fa_rope_full .py:1169-1170).
+
+    With the reference's four positional arguments this behaves like the
+    reference. ``has_cls`` and ``H_img`` are keyword extensions; ``H_img``
+    defaults to the side of ``cos_sin``'s table (14 for the reference's 14x14 grid).
+    """
+    if H_img is None:
+        n_pos = cos_sin.tables()[0].shape[0]
+        H_img = math.isqrt(n_pos)
+    return TritonAttention.apply(Q, K, V, cos_sin, H_img, has_cls)

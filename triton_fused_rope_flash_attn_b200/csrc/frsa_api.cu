@@ -1,0 +1,179 @@
+// C ABI (include/frsa.h): argument validation, TMA tensor-map encoding and
+// dispatch to the sm_100a kernels. This is the library's only translation
+// unit; the kernel files are included so that the device status word is one
+// symbol without relocatable device code.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "../../include/frsa.h"
+#include "frsa_internal.h"
+#include "frsa_ptx.cuh"
+
+#include "frsa_bwd.cu"
+#include "frsa_fwd.cu"
+
+namespace {
+
+using frsa::kTile;
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Is the current device an sm_100 part? Cached per device ordinal.
+bool device_is_sm100() {
+  static int cache[64];  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (dev < 0 || dev >= 64) return false;
+  if (cache[dev] == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cache[dev] = (major == 10 && minor == 0) ? 1 : 2;
+  }
+  return cache[dev] == 1;
+}
+
+// 3-D map over a contiguous [BH, N, D] 16-bit tensor: dims {D, N, BH}, box
+// {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor.
+bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(s.D), static_cast<cuuint64_t>(s.N),
+                              static_cast<cuuint64_t>(s.BH)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.D) * 2,
+                                 static_cast<cuuint64_t>(s.D) * s.N * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, s.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
+  if (!a) return FRSA_ERR_NULL_ARG;
+  if (!a->q || !a->k || !a->v || !a->cosp || !a->sinp) return FRSA_ERR_NULL_ARG;
+  if (a->B < 1 || a->H < 1 || a->N < 1 || a->D < 1) return FRSA_ERR_BAD_SHAPE;
+  if (a->has_cls != 0 && a->has_cls != 1) return FRSA_ERR_BAD_SHAPE;
+  if (a->D % 8 != 0 || a->D > 128) return FRSA_ERR_UNSUPPORTED_D;
+  if (a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;  // table must cover every token
+  const long long BH = static_cast<long long>(a->B) * a->H;
+  const long long nqt = (a->N + kTile - 1) / kTile;
+  if (BH * nqt > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
+  if (a->io_dtype != a->compute_dtype) return FRSA_ERR_UNSUPPORTED_DTYPE;
+  if (a->compute_dtype != FRSA_DTYPE_BF16 && a->compute_dtype != FRSA_DTYPE_F16)
+    return FRSA_ERR_UNSUPPORTED_DTYPE;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) ||
+      !aligned16(a->sinp))
+    return FRSA_ERR_MISALIGNED;
+  s->BH = static_cast<int>(BH);
+  s->N = static_cast<int>(a->N);
+  s->D = static_cast<int>(a->D);
+  s->has_cls = a->has_cls;
+  s->scale = a->scale;
+  s->bf16 = a->compute_dtype == FRSA_DTYPE_BF16;
+  return FRSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int frsa_abi_version(void) { return FRSA_ABI_VERSION; }
+
+const char* frsa_strerror(int code) {
+  switch (code) {
+    case FRSA_OK: return "ok";
+    case FRSA_ERR_NULL_ARG: return "frsa: a required pointer is NULL";
+    case FRSA_ERR_BAD_SHAPE: return "frsa: bad shape (B, H, N, D, has_cls or table size)";
+    case FRSA_ERR_UNSUPPORTED_D: return "frsa: head dim must be a multiple of 8 and at most 128";
+    case FRSA_ERR_UNSUPPORTED_DTYPE: return "frsa: unsupported dtype combination";
+    case FRSA_ERR_MISALIGNED: return "frsa: a tensor pointer is not 16-byte aligned";
+    case FRSA_ERR_LAUNCH: return "frsa: CUDA launch or tensor-map encode failed";
+    case FRSA_ERR_DEVICE_TIMEOUT: return "frsa: a kernel timed out on a bounded wait";
+    case FRSA_ERR_NO_DEVICE: return "frsa: the current CUDA device is not sm_100";
+    case FRSA_ERR_WORKSPACE: return "frsa: backward workspace missing or too small";
+    default: return "frsa: unknown error";
+  }
+}
+
+size_t frsa_bwd_workspace_bytes(const frsa_attn_args* a) {
+  frsa::LaunchShape s;
+  if (validate_common(a, &s) != FRSA_OK) return 0;
+  if (!frsa::bwd_needs_workspace(s)) return 0;
+  return static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
+}
+
+int frsa_fwd(const frsa_attn_args* a, void* stream) {
+  frsa::LaunchShape s;
+  int rc = validate_common(a, &s);
+  if (rc != FRSA_OK) return rc;
+  if (!a->o || !a->lse) return FRSA_ERR_NULL_ARG;
+  if (!aligned16(a->o) || !aligned16(a->lse)) return FRSA_ERR_MISALIGNED;
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  CUtensorMap tq, tk, tv;
+  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s))
+    return FRSA_ERR_LAUNCH;
+  const cudaError_t e = frsa::launch_fwd(s, tq, tk, tv, a->cosp, a->sinp, a->o, a->lse,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : FRSA_ERR_LAUNCH;
+}
+
+int frsa_bwd(const frsa_attn_args* a, void* stream) {
+  frsa::LaunchShape s;
+  int rc = validate_common(a, &s);
+  if (rc != FRSA_OK) return rc;
+  if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv || !a->delta)
+    return FRSA_ERR_NULL_ARG;
+  if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||
+      !aligned16(a->dv) || !aligned16(a->lse) || !aligned16(a->delta))
+    return FRSA_ERR_MISALIGNED;
+  float* ws = nullptr;
+  if (frsa::bwd_needs_workspace(s)) {
+    const size_t need = static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
+    if (!a->workspace || a->workspace_bytes < need) return FRSA_ERR_WORKSPACE;
+    if (!aligned16(a->workspace)) return FRSA_ERR_MISALIGNED;
+    ws = static_cast<float*>(a->workspace);
+  }
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  CUtensorMap tq, tk, tv, tdo;
+  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
+      !encode_map(&tdo, a->d_o, s))
+    return FRSA_ERR_LAUNCH;
+  const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, a->o, a->d_o, a->lse, a->delta,
+                                         a->cosp, a->sinp, a->dq, a->dk, a->dv, ws,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : FRSA_ERR_LAUNCH;
+}
+
+int frsa_query_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return FRSA_ERR_LAUNCH;
+  int st = 0;
+  if (cudaMemcpyFromSymbol(&st, frsa::g_dev_status, sizeof(int)) != cudaSuccess)
+    return FRSA_ERR_LAUNCH;
+  if (st != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(frsa::g_dev_status, &zero, sizeof(int));
+    return FRSA_ERR_DEVICE_TIMEOUT;
+  }
+  return FRSA_OK;
+}
+
+}  // extern "C"

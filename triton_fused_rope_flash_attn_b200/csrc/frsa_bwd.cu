@@ -1,0 +1,548 @@
+// Backward kernels: dQ, dK, dV of softmax(R(Q) R(K)^T * scale) V.
+//
+// Restates _attn_bwd_preprocess, _attn_bwd_dk_dv_rope and _attn_bwd_dq_rope
+// (fa_rope_full .py:325-357, 374-691, 708-1009) as:
+//
+//   delta_kernel  Delta = rowsum(dO * O) in f32 (fa_rope_full .py:352-357).
+//   bwd_kernel    key-major tcgen05 kernel. A CTA owns 128-key tiles of one
+//                 (batch*head) and loops over all 128-query tiles:
+//                   S^T  = K^ Q^T            (TMEM, f32)
+//                   dP^T = V dO^T            (TMEM, f32)
+//                   P    = exp2(S^T c2 - lse2_q),  dS = P (dP - Delta_q)  (registers)
+//                   dV  += P dO,  dK^ += dS Q^  (TMEM accumulators)
+//                   dQ^ += dS^T K^           (TMEM)
+//                 P and dS are written once to shared memory as [key][query]
+//                 tiles; the dQ product reads the same dS tile query-major.
+//                 "Resident" mode (N <= 256, D <= 64): one CTA per head walks
+//                 every key tile and keeps both dQ^ tiles in TMEM, so dQ is
+//                 finished on chip with no atomics (deterministic).
+//                 "Atomic" mode (any N): one CTA per (head, key tile); each
+//                 dQ^ partial is scaled and added into an f32 workspace.
+//   dq_finalize   (atomic mode) dQ = R^T dQ^ rounded to the I/O type.
+//
+// Compared with the reference, S and dP are computed once per (key tile,
+// query tile) pair instead of twice, and no separate dQ pass recomputes them.
+//
+// Warp roles in bwd_kernel: warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2..5 the row warpgroup (thread = key row of the tile; for dQ
+// read-back thread = query row).
+//
+// TMEM columns: [0,128) S^T, [128,256) dP^T (atomic mode: reused for the dQ^
+// partial), [256, 256+DP) dV, [256+DP, 256+2DP) dK^, resident mode:
+// [384 + 64 i, 448 + 64 i) dQ^ of query tile i.
+#include "frsa_internal.h"
+#include "frsa_ptx.cuh"
+#include "frsa_rope.cuh"
+
+namespace frsa {
+
+namespace {
+
+constexpr int kBwdThreads = 192;
+constexpr uint32_t kTmemColsBwd = 512;
+
+template <int NCH>
+struct BwdSmem {
+  static constexpr int KVS = (NCH == 1) ? 2 : 1;  // key/value tile stages
+  static constexpr int QS = (NCH == 1) ? 2 : 1;   // query/dO tile stages
+  uint8_t k[KVS][NCH][kChunkBytes];
+  uint8_t v[KVS][NCH][kChunkBytes];
+  uint8_t q[QS][NCH][kChunkBytes];
+  uint8_t dO[QS][NCH][kChunkBytes];
+  uint8_t p[2][kChunkBytes];   // P  [128 key][128 query], two 64-column chunks
+  uint8_t ds[2][kChunkBytes];  // dS [128 key][128 query]
+  float lse2[QS][kTile];       // lse * log2(e) of the query tile
+  float delta[QS][kTile];
+  uint64_t kv_full[KVS], kv_empty[KVS];
+  uint64_t q_full[QS], q_empty[QS];
+  uint64_t kq_ready, st_full, ds_full, mm_done, tm_free, acc_free;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct BwdParams {
+  const float* cosp;
+  const float* sinp;
+  const float* lse;
+  const float* delta;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* dq_accum;
+  int N, D, nqt, nkv, has_cls;
+  float c2;     // scale * log2(e)
+  float scale;
+};
+
+template <typename T, int NCH, bool RESIDENT>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               const BwdParams prm) {
+  using Sm = BwdSmem<NCH>;
+  constexpr int KVS = Sm::KVS;
+  constexpr int QS = Sm::QS;
+  static_assert(!RESIDENT || NCH == 1, "resident mode keeps two dQ tiles of <= 64 columns");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Sm* smp = aligned_smem<Sm>(smem_raw);
+  if (smp == nullptr) return;
+  Sm& sm = *smp;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int N = prm.N, D = prm.D;
+  const int DP = (D + 15) & ~15;
+  const int ksteps = DP >> 4;
+  const int nqt = prm.nqt;
+  int bh, j0, nj;
+  if (RESIDENT) {
+    bh = blockIdx.x;
+    j0 = 0;
+    nj = prm.nkv;
+  } else {
+    bh = blockIdx.x / prm.nkv;
+    j0 = blockIdx.x - bh * prm.nkv;
+    nj = 1;
+  }
+  volatile int* abort_flag = &sm.abort_flag;
+
+  if (threadIdx.x == 0) {
+    sm.abort_flag = 0;
+    for (int s = 0; s < KVS; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int s = 0; s < QS; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
+    }
+    mbar_init(&sm.kq_ready, 1);
+    mbar_init(&sm.st_full, 1);
+    mbar_init(&sm.ds_full, 1);
+    mbar_init(&sm.mm_done, 1);
+    mbar_init(&sm.tm_free, 1);
+    mbar_init(&sm.acc_free, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemColsBwd);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + DP;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      int qi = 0;
+      for (int jj = 0; jj < nj; ++jj) {
+        const int j = j0 + jj, ks = jj % KVS;
+        mbar_wait(&sm.kv_empty[ks], ((jj / KVS) & 1) ^ 1, abort_flag);
+        mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+          tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+        }
+        for (int i = 0; i < nqt; ++i) {
+          if (RESIDENT && jj > 0) continue;
+          const int qs = RESIDENT ? i : qi % QS;
+          mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
+          for (int c = 0; c < NCH; ++c) {
+            tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+            tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+          }
+          ++qi;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr bool kBf = Elt<T>::kBf16;
+      const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);   // S^T, dP^T
+      const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
+      const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
+      int it = 0, qi = 0;
+      for (int jj = 0; jj < nj; ++jj) {
+        const int ks = jj % KVS;
+        for (int i = 0; i < nqt; ++i) {
+          const bool fresh = !(RESIDENT && jj > 0);
+          const int qs = RESIDENT ? i : qi % QS;
+          mbar_wait(&sm.kq_ready, it & 1, abort_flag);
+          tc_fence_after();
+          if (it > 0) {
+            mbar_wait(&sm.tm_free, (it - 1) & 1, abort_flag);
+            tc_fence_after();
+          }
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const int c = kk >> 2;
+            const uint32_t koff = (kk & 3) * 32;
+            mma_ss(tST, sw128_desc(smem_u32(sm.k[ks][c]) + koff, 16, 1024),
+                   sw128_desc(smem_u32(sm.q[qs][c]) + koff, 16, 1024), idS, kk > 0);
+          }
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const int c = kk >> 2;
+            const uint32_t koff = (kk & 3) * 32;
+            mma_ss(tDPT, sw128_desc(smem_u32(sm.v[ks][c]) + koff, 16, 1024),
+                   sw128_desc(smem_u32(sm.dO[qs][c]) + koff, 16, 1024), idS, kk > 0);
+          }
+          mma_commit(&sm.st_full);
+          mbar_wait(&sm.ds_full, it & 1, abort_flag);
+          tc_fence_after();
+          if (i == 0 && jj > 0) {
+            mbar_wait(&sm.acc_free, (jj - 1) & 1, abort_flag);
+            tc_fence_after();
+          }
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint32_t aoff = (kk & 3) * 32;
+            const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
+            // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
+            mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
+                   sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
+            // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
+            mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
+                   sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
+          }
+          // dQ^ (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
+          const uint32_t tDQ = RESIDENT ? (tmem + 384 + 64 * i) : tDPT;
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint32_t acc = RESIDENT ? ((jj == 0 && kk == 0) ? 0u : 1u) : (kk > 0 ? 1u : 0u);
+            mma_ss(tDQ, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
+                   sw128_desc(smem_u32(sm.k[ks][0]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
+          }
+          mma_commit(&sm.mm_done);
+          if (!RESIDENT) mma_commit(&sm.q_empty[qs]);
+          if (i == nqt - 1) mma_commit(&sm.kv_empty[ks]);
+          ++it;
+          if (fresh) ++qi;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ row warpgroup
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const int tid = threadIdx.x - 64;
+    const float c2 = prm.c2;
+    const size_t head_row0 = static_cast<size_t>(bh) * N;
+    int it = 0, qi = 0;
+    for (int jj = 0; jj < nj; ++jj) {
+      const int j = j0 + jj, ks = jj % KVS;
+      const int kv0 = j * kTile;
+      const bool kv_valid = (kv0 + r) < N;
+      mbar_wait(&sm.kv_full[ks], (jj / KVS) & 1, abort_flag);
+      rotate_row_smem<T, NCH>(&sm.k[ks][0][0], r, D, rope_pos(kv0 + r, N, prm.has_cls), prm.cosp,
+                              prm.sinp);
+      for (int i = 0; i < nqt; ++i) {
+        const int q0 = i * kTile;
+        const bool fresh = !(RESIDENT && jj > 0);
+        const int qs = RESIDENT ? i : qi % QS;
+        if (fresh) {
+          mbar_wait(&sm.q_full[qs], (qi / QS) & 1, abort_flag);
+          rotate_row_smem<T, NCH>(&sm.q[qs][0][0], r, D, rope_pos(q0 + r, N, prm.has_cls),
+                                  prm.cosp, prm.sinp);
+          const bool qv = (q0 + r) < N;
+          sm.lse2[qs][r] = qv ? prm.lse[head_row0 + q0 + r] * 1.4426950408889634f : 0.f;
+          sm.delta[qs][r] = qv ? prm.delta[head_row0 + q0 + r] : 0.f;
+          ++qi;
+        }
+        fence_proxy_async_smem();
+        named_bar(1, 128);
+        if (tid == 0) mbar_arrive(&sm.kq_ready);
+
+        mbar_wait(&sm.st_full, it & 1, abort_flag);
+        tc_fence_after();
+        if (it > 0) mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);  // P/dS tiles free
+        const int nqv = N - q0;  // valid query columns in this tile (may exceed 128)
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float sv[32], dp[32];
+          tmem_ld32(tST + lane_off + cc * 32, sv);
+          tmem_ld32(tDPT + lane_off + cc * 32, dp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int qc = cc * 32 + c;
+            const float pv =
+                (kv_valid && qc < nqv) ? ex2(fmaf(sv[c], c2, -sm.lse2[qs][qc])) : 0.f;
+            sv[c] = pv;
+            dp[c] = pv * (dp[c] - sm.delta[qs][qc]);
+          }
+          uint8_t* pch = sm.p[cc >> 1];
+          uint8_t* dch = sm.ds[cc >> 1];
+#pragma unroll
+          for (int g4 = 0; g4 < 4; ++g4) {
+            const uint32_t off = sw128_off(r, (cc & 1) * 4 + g4);
+            uint4 w;
+            w.x = Elt<T>::pack(sv[g4 * 8 + 0], sv[g4 * 8 + 1]);
+            w.y = Elt<T>::pack(sv[g4 * 8 + 2], sv[g4 * 8 + 3]);
+            w.z = Elt<T>::pack(sv[g4 * 8 + 4], sv[g4 * 8 + 5]);
+            w.w = Elt<T>::pack(sv[g4 * 8 + 6], sv[g4 * 8 + 7]);
+            *reinterpret_cast<uint4*>(pch + off) = w;
+            w.x = Elt<T>::pack(dp[g4 * 8 + 0], dp[g4 * 8 + 1]);
+            w.y = Elt<T>::pack(dp[g4 * 8 + 2], dp[g4 * 8 + 3]);
+            w.z = Elt<T>::pack(dp[g4 * 8 + 4], dp[g4 * 8 + 5]);
+            w.w = Elt<T>::pack(dp[g4 * 8 + 6], dp[g4 * 8 + 7]);
+            *reinterpret_cast<uint4*>(dch + off) = w;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        named_bar(1, 128);
+        if (tid == 0) {
+          mbar_arrive(&sm.ds_full);
+          if (RESIDENT) mbar_arrive(&sm.tm_free);
+        }
+        if (!RESIDENT) {
+          // dQ^ partial of this (key tile, query tile): scale and add into the workspace.
+          mbar_wait(&sm.mm_done, it & 1, abort_flag);
+          tc_fence_after();
+          const int qrow = q0 + r;
+#pragma unroll 1
+          for (int c16 = 0; c16 < 8; ++c16) {
+            if (c16 * 16 < DP) {
+              float v[16];
+              tmem_ld16(tDPT + lane_off + c16 * 16, v);
+              tmem_wait_ld();
+              if (qrow < N) {
+                float4* dst = reinterpret_cast<float4*>(prm.dq_accum + (head_row0 + qrow) * D +
+                                                        c16 * 16);
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                  if (c16 * 16 + g * 4 < D)
+                    atomicAdd(dst + g, make_float4(v[4 * g] * prm.scale, v[4 * g + 1] * prm.scale,
+                                                   v[4 * g + 2] * prm.scale,
+                                                   v[4 * g + 3] * prm.scale));
+                }
+              }
+            }
+          }
+          tc_fence_before();
+          named_bar(1, 128);
+          if (tid == 0) mbar_arrive(&sm.tm_free);
+        }
+        ++it;
+      }
+      // dV, dK epilogue of key tile j
+      mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
+      tc_fence_after();
+      {
+        float acc[64 * NCH];
+#pragma unroll
+        for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+          if (c16 * 16 < DP) {
+            float v[16];
+            tmem_ld16(tDV + lane_off + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e];
+          }
+        }
+        if (kv_valid)
+          store_row<T, 64 * NCH>(reinterpret_cast<T*>(prm.dv) + (head_row0 + kv0 + r) * D, acc, D);
+#pragma unroll
+        for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+          if (c16 * 16 < DP) {
+            float v[16];
+            tmem_ld16(tDK + lane_off + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e] * prm.scale;
+          }
+        }
+        if (kv_valid) {
+          unrotate_row_regs<64 * NCH>(acc, D, rope_pos(kv0 + r, N, prm.has_cls), prm.cosp,
+                                      prm.sinp);
+          store_row<T, 64 * NCH>(reinterpret_cast<T*>(prm.dk) + (head_row0 + kv0 + r) * D, acc, D);
+        }
+      }
+      tc_fence_before();
+      named_bar(1, 128);
+      if (tid == 0) mbar_arrive(&sm.acc_free);
+    }
+    if (RESIDENT) {
+      // dQ epilogue: every MMA has completed (last mm_done waited above).
+      for (int i = 0; i < nqt; ++i) {
+        const int qrow = i * kTile + r;
+        float acc[64];
+#pragma unroll
+        for (int c16 = 0; c16 < 4; ++c16) {
+          if (c16 * 16 < DP) {
+            float v[16];
+            tmem_ld16(tmem + 384 + 64 * i + lane_off + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e] * prm.scale;
+          }
+        }
+        if (qrow < N) {
+          unrotate_row_regs<64>(acc, D, rope_pos(qrow, N, prm.has_cls), prm.cosp, prm.sinp);
+          store_row<T, 64>(reinterpret_cast<T*>(prm.dq) + (head_row0 + qrow) * D, acc, D);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemColsBwd);
+  }
+}
+
+// Delta[row] = sum_d O[row, d] dO[row, d] in f32; 16 threads per row.
+template <typename T>
+__global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ d_o,
+                             float* __restrict__ delta, long long rows, int D) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  float acc = 0.f;
+  if (row < rows) {
+    const uint4* po = reinterpret_cast<const uint4*>(o + row * D);
+    const uint4* pd = reinterpret_cast<const uint4*>(d_o + row * D);
+    for (int g = sub; g < (D >> 3); g += 16) {
+      const uint4 a = __ldg(po + g), b = __ldg(pd + g);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
+        acc = fmaf(x.x, y.x, acc);
+        acc = fmaf(x.y, y.y, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off, 16);
+  if (row < rows && sub == 0) delta[row] = acc;
+}
+
+// dQ = R^T dQ^ (dQ^ already scaled), one thread per 8 columns.
+template <typename T>
+__global__ void dq_finalize_kernel(const float* __restrict__ acc, T* __restrict__ dq,
+                                   const float* __restrict__ cosp, const float* __restrict__ sinp,
+                                   long long rows, int N, int D, int has_cls) {
+  const int gpr = D >> 3;
+  const long long gidx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gidx >= rows * gpr) return;
+  const long long row = gidx / gpr;
+  const int g = static_cast<int>(gidx - row * gpr);
+  const int t = static_cast<int>(row % N);
+  const float4* src = reinterpret_cast<const float4*>(acc + row * D + g * 8);
+  float v[8];
+  const float4 a = src[0], b = src[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  const int pos = rope_pos(t, N, has_cls);
+  if (pos >= 0) {
+    const int D2 = D >> 1;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float c = __ldg(cosp + static_cast<size_t>(pos) * D2 + g * 4 + p);
+      const float s = __ldg(sinp + static_cast<size_t>(pos) * D2 + g * 4 + p);
+      const float e = v[2 * p], od = v[2 * p + 1];
+      v[2 * p] = e * c + od * s;
+      v[2 * p + 1] = od * c - e * s;
+    }
+  }
+  uint4 w;
+  w.x = Elt<T>::pack(v[0], v[1]);
+  w.y = Elt<T>::pack(v[2], v[3]);
+  w.z = Elt<T>::pack(v[4], v[5]);
+  w.w = Elt<T>::pack(v[6], v[7]);
+  reinterpret_cast<uint4*>(dq + row * D)[g] = w;
+}
+
+}  // namespace
+
+bool bwd_needs_workspace(const LaunchShape& s) { return !(s.N <= 2 * kTile && s.D <= 64); }
+
+namespace {
+
+template <typename T, int NCH, bool RESIDENT>
+cudaError_t launch_bwd_main(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                            const CUtensorMap& tm_v, const CUtensorMap& tm_do,
+                            const BwdParams& p, cudaStream_t stream) {
+  const size_t smem = sizeof(BwdSmem<NCH>) + 1024;
+  auto kern = bwd_kernel<T, NCH, RESIDENT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const long long grid = RESIDENT ? static_cast<long long>(s.BH)
+                                  : static_cast<long long>(s.BH) * p.nkv;
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                         const CUtensorMap& tm_v, const CUtensorMap& tm_do, const void* o,
+                         const void* d_o, const float* lse, float* delta, const float* cosp,
+                         const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
+                         cudaStream_t stream) {
+  const long long rows = static_cast<long long>(s.BH) * s.N;
+  {
+    const int threads = 256;
+    const long long blocks = (rows * 16 + threads - 1) / threads;
+    delta_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+        static_cast<const T*>(o), static_cast<const T*>(d_o), delta, rows, s.D);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  BwdParams p;
+  p.cosp = cosp;
+  p.sinp = sinp;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.dq_accum = dq_accum;
+  p.N = s.N;
+  p.D = s.D;
+  p.nqt = (s.N + kTile - 1) / kTile;
+  p.nkv = p.nqt;
+  p.has_cls = s.has_cls;
+  p.c2 = s.scale * 1.4426950408889634f;
+  p.scale = s.scale;
+  cudaError_t e;
+  if (!bwd_needs_workspace(s)) {
+    return launch_bwd_main<T, 1, true>(s, tm_q, tm_k, tm_v, tm_do, p, stream);
+  }
+  e = cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
+  if (e != cudaSuccess) return e;
+  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream)
+                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream);
+  if (e != cudaSuccess) return e;
+  const int threads = 256;
+  const long long total = rows * (s.D >> 3);
+  dq_finalize_kernel<T><<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
+                          stream>>>(dq_accum, static_cast<T*>(dq), cosp, sinp, rows, s.N, s.D,
+                                    s.has_cls);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const void* o,
+                       const void* d_o, const float* lse, float* delta, const float* cosp,
+                       const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
+                       cudaStream_t stream) {
+  if (s.bf16)
+    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, o, d_o, lse, delta, cosp, sinp,
+                                       dq, dk, dv, dq_accum, stream);
+  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, o, d_o, lse, delta, cosp, sinp, dq, dk,
+                              dv, dq_accum, stream);
+}
+
+}  // namespace frsa

@@ -1,0 +1,38 @@
+// Internal launcher interface shared by the C-ABI layer and the kernel files.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace frsa {
+
+// Tile geometry shared by every kernel: 128-row tiles, 64-column (128-byte)
+// swizzle chunks of 16-bit elements.
+constexpr int kTile = 128;
+constexpr int kChunkCols = 64;
+constexpr int kChunkBytes = kTile * kChunkCols * 2;  // 16 KiB
+
+struct LaunchShape {
+  int BH;        // B * H
+  int N;         // sequence length
+  int D;         // head dim (multiple of 8, <= 128)
+  int has_cls;
+  float scale;
+  bool bf16;     // true: bf16, false: f16
+};
+
+// Forward. tm_q/k/v: 3-D maps {D, N, BH} with box {64, 128, 1}, 128B swizzle.
+cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                       const CUtensorMap& tm_v, const float* cosp, const float* sinp, void* o,
+                       float* lse, cudaStream_t stream);
+
+// Backward (delta preprocess + main kernel + optional dQ finalize).
+// dq_accum: fp32 [BH, N, D] workspace or nullptr when bwd_needs_workspace() is false.
+bool bwd_needs_workspace(const LaunchShape& s);
+cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const void* o,
+                       const void* d_o, const float* lse, float* delta, const float* cosp,
+                       const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
+                       cudaStream_t stream);
+
+}  // namespace frsa
