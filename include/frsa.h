@@ -65,7 +65,7 @@ typedef struct frsa_attn_args {
   void* dq;
   void* dk;
   void* dv;
-  float* delta;       /* fp32 [B, H, N] scratch: rowsum(dO * O) */
+  float* delta;       /* optional fp32 [B, H, N]: receives rowsum(dO * O) when non-NULL */
   void* workspace;    /* fp32 scratch of frsa_bwd_workspace_bytes() bytes, or NULL when that is 0 */
   size_t workspace_bytes;
   /* RoPE pair tables */
@@ -87,7 +87,9 @@ int frsa_fwd(const frsa_attn_args* args, void* stream);
 /* Backward: dQ, dK, dV from d_o, o, lse (and q, k, v, tables).
  * Replaces the three launches of TritonAttention.backward
  * (_attn_bwd_preprocess fa_rope_full .py:1076-1082, _attn_bwd_dk_dv_rope
- * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136). */
+ * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136)
+ * with one kernel (N <= 256 and D <= 64), or with a workspace clear, one
+ * kernel and a dQ finalize pass otherwise. */
 int frsa_bwd(const frsa_attn_args* args, void* stream);
 
 /* Bytes of fp32 workspace frsa_bwd needs for this shape (0 when the whole
@@ -97,6 +99,10 @@ size_t frsa_bwd_workspace_bytes(const frsa_attn_args* args);
 
 /* Message for an FRSA_ERR_* code (static storage). */
 const char* frsa_strerror(int code);
+
+/* Detail (CUDA error string and call) of the last FRSA_ERR_LAUNCH returned on
+ * the calling host thread; "" if none. No reference counterpart. */
+const char* frsa_last_error_detail(void);
 
 /* Synchronizes the current device, returns FRSA_ERR_DEVICE_TIMEOUT if any
  * kernel recorded a bounded-wait timeout since the last call (and clears it),

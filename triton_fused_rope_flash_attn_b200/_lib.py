@@ -21,6 +21,7 @@ EXPORTED_SYMBOLS = (
     "frsa_strerror",
     "frsa_query_status",
     "frsa_abi_version",
+    "frsa_last_error_detail",
 )
 
 
@@ -59,7 +60,9 @@ class FrsaError(RuntimeError):
 
     def __init__(self, code: int, where: str):
         self.code = code
-        super().__init__(f"{where}: {strerror(code)} (code {code})")
+        detail = load().frsa_last_error_detail().decode() if code == 6 else ""
+        super().__init__(f"{where}: {strerror(code)} (code {code})" +
+                         (f" [{detail}]" if detail else ""))
 
 
 _LIB = None
@@ -86,6 +89,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.frsa_strerror.restype = ctypes.c_char_p
     lib.frsa_query_status.argtypes = []
     lib.frsa_query_status.restype = ctypes.c_int
+    lib.frsa_last_error_detail.argtypes = []
+    lib.frsa_last_error_detail.restype = ctypes.c_char_p
     lib.frsa_abi_version.argtypes = []
     lib.frsa_abi_version.restype = ctypes.c_int
     if path is None:

@@ -87,16 +87,19 @@ def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True):
     return o, lse
 
 
-def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = True):
-    """Backward through the C ABI. Returns ``(dq, dk, dv)`` in ``q.dtype``."""
+def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = True,
+                             delta_out=None):
+    """Backward through the C ABI. Returns ``(dq, dk, dv)`` in ``q.dtype``.
+
+    ``delta_out`` (optional float32 ``[B, H, N]``) receives ``rowsum(dO * O)``.
+    """
     comp = q.dtype
     q, k, v, o, d_o = (t.contiguous() for t in (q, k, v, o, d_o))
     cosp, sinp = cosp.contiguous(), sinp.contiguous()
     B, H, N, D = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    delta = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, d_o=d_o, dq=dq, dk=dk,
-                   dv=dv, delta=delta)
+                   dv=dv, delta=delta_out)
     lib = _lib.load()
     ws_bytes = lib.frsa_bwd_workspace_bytes(a)
     ws = None

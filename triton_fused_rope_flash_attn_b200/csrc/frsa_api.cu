@@ -4,6 +4,7 @@
 // symbol without relocatable device code.
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -32,11 +33,15 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// Is the current device an sm_100 part? Cached per device ordinal.
+// Is the current device an sm_100 part? Cached per device ordinal. Also makes
+// the device's primary context current on this host thread: the tensor-map
+// encoder is a driver call and needs it, and a thread that has not touched the
+// runtime yet (autograd's backward worker, a user thread) may have none.
 bool device_is_sm100() {
   static int cache[64];  // 0 unknown, 1 yes, 2 no
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaSetDevice(dev) != cudaSuccess) return false;
   if (dev < 0 || dev >= 64) return false;
   if (cache[dev] == 0) {
     int major = 0, minor = 0;
@@ -46,6 +51,8 @@ bool device_is_sm100() {
   }
   return cache[dev] == 1;
 }
+
+thread_local int g_last_encode_result = 0;
 
 // 3-D map over a contiguous [BH, N, D] 16-bit tensor: dims {D, N, BH}, box
 // {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor.
@@ -62,7 +69,21 @@ bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s) {
                         3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
   return r == CUDA_SUCCESS;
+}
+
+// Detail of the last FRSA_ERR_LAUNCH on this host thread.
+thread_local char g_last_detail[256] = "";
+
+int launch_error(const char* where, cudaError_t e) {
+  if (e == cudaSuccess)
+    snprintf(g_last_detail, sizeof(g_last_detail), "%s: tensor-map encode failed (CUresult %d)",
+             where, g_last_encode_result);
+  else
+    snprintf(g_last_detail, sizeof(g_last_detail), "%s: %s (%d)", where, cudaGetErrorString(e),
+             static_cast<int>(e));
+  return FRSA_ERR_LAUNCH;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -128,22 +149,25 @@ int frsa_fwd(const frsa_attn_args* a, void* stream) {
   if (!a->o || !a->lse) return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->lse)) return FRSA_ERR_MISALIGNED;
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  // A non-sticky error left on this host thread by an earlier runtime call
+  // (e.g. cudaErrorNotReady from an event poll) must not be blamed on our launch.
+  (void)cudaGetLastError();
   CUtensorMap tq, tk, tv;
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s))
-    return FRSA_ERR_LAUNCH;
+    return launch_error("frsa_fwd", cudaSuccess);
   const cudaError_t e = frsa::launch_fwd(s, tq, tk, tv, a->cosp, a->sinp, a->o, a->lse,
                                          static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? FRSA_OK : FRSA_ERR_LAUNCH;
+  return e == cudaSuccess ? FRSA_OK : launch_error("frsa_fwd", e);
 }
 
 int frsa_bwd(const frsa_attn_args* a, void* stream) {
   frsa::LaunchShape s;
   int rc = validate_common(a, &s);
   if (rc != FRSA_OK) return rc;
-  if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv || !a->delta)
+  if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv)
     return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||
-      !aligned16(a->dv) || !aligned16(a->lse) || !aligned16(a->delta))
+      !aligned16(a->dv) || !aligned16(a->lse))
     return FRSA_ERR_MISALIGNED;
   float* ws = nullptr;
   if (frsa::bwd_needs_workspace(s)) {
@@ -153,15 +177,18 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
     ws = static_cast<float*>(a->workspace);
   }
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  (void)cudaGetLastError();  // see frsa_fwd
   CUtensorMap tq, tk, tv, tdo;
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
       !encode_map(&tdo, a->d_o, s))
-    return FRSA_ERR_LAUNCH;
+    return launch_error("frsa_bwd", cudaSuccess);
   const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, a->o, a->d_o, a->lse, a->delta,
                                          a->cosp, a->sinp, a->dq, a->dk, a->dv, ws,
                                          static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? FRSA_OK : FRSA_ERR_LAUNCH;
+  return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);
 }
+
+const char* frsa_last_error_detail(void) { return g_last_detail; }
 
 int frsa_query_status(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FRSA_ERR_LAUNCH;

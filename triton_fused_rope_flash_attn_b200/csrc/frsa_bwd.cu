@@ -3,8 +3,10 @@
 // Restates _attn_bwd_preprocess, _attn_bwd_dk_dv_rope and _attn_bwd_dq_rope
 // (fa_rope_full .py:325-357, 374-691, 708-1009) as:
 //
-//   delta_kernel  Delta = rowsum(dO * O) in f32 (fa_rope_full .py:352-357).
-//   bwd_kernel    key-major tcgen05 kernel. A CTA owns 128-key tiles of one
+//   bwd_kernel    key-major tcgen05 kernel. When a query tile arrives the row
+//                 warpgroup first forms Delta = rowsum(dO * O) in f32 from the
+//                 dO tile in shared memory and the O row in global memory
+//                 (fa_rope_full .py:352-357), so no separate preprocess launch. A CTA owns 128-key tiles of one
 //                 (batch*head) and loops over all 128-query tiles:
 //                   S^T  = K^ Q^T            (TMEM, f32)
 //                   dP^T = V dO^T            (TMEM, f32)
@@ -64,7 +66,8 @@ struct BwdParams {
   const float* cosp;
   const float* sinp;
   const float* lse;
-  const float* delta;
+  const void* o;
+  float* delta_out;  // optional: receives Delta when non-null
   void* dq;
   void* dk;
   void* dv;
@@ -252,7 +255,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                   prm.cosp, prm.sinp);
           const bool qv = (q0 + r) < N;
           sm.lse2[qs][r] = qv ? prm.lse[head_row0 + q0 + r] * 1.4426950408889634f : 0.f;
-          sm.delta[qs][r] = qv ? prm.delta[head_row0 + q0 + r] : 0.f;
+          float dl = 0.f;
+          if (qv) {
+            // Delta = sum_d O dO over this query row (dO from the swizzled tile).
+            const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const T*>(prm.o) +
+                                                               (head_row0 + q0 + r) * D);
+#pragma unroll
+            for (int gg = 0; gg < 8 * NCH; ++gg) {
+              if (gg * 8 < D) {
+                const uint4 a = __ldg(orow + gg);
+                const uint4 b = *reinterpret_cast<const uint4*>(&sm.dO[qs][gg >> 3][0] +
+                                                                 sw128_off(r, gg & 7));
+                const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
+                  dl = fmaf(x.x, y.x, dl);
+                  dl = fmaf(x.y, y.y, dl);
+                }
+              }
+            }
+            if (prm.delta_out != nullptr && j0 == 0 && jj == 0)
+              prm.delta_out[head_row0 + q0 + r] = dl;
+          }
+          sm.delta[qs][r] = dl;
           ++qi;
         }
         fence_proxy_async_smem();
@@ -400,32 +426,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// Delta[row] = sum_d O[row, d] dO[row, d] in f32; 16 threads per row.
-template <typename T>
-__global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ d_o,
-                             float* __restrict__ delta, long long rows, int D) {
-  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-  const int sub = threadIdx.x & 15;
-  float acc = 0.f;
-  if (row < rows) {
-    const uint4* po = reinterpret_cast<const uint4*>(o + row * D);
-    const uint4* pd = reinterpret_cast<const uint4*>(d_o + row * D);
-    for (int g = sub; g < (D >> 3); g += 16) {
-      const uint4 a = __ldg(po + g), b = __ldg(pd + g);
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
-        acc = fmaf(x.x, y.x, acc);
-        acc = fmaf(x.y, y.y, acc);
-      }
-    }
-  }
-#pragma unroll
-  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off, 16);
-  if (row < rows && sub == 0) delta[row] = acc;
-}
-
 // dQ = R^T dQ^ (dQ^ already scaled), one thread per 8 columns.
 template <typename T>
 __global__ void dq_finalize_kernel(const float* __restrict__ acc, T* __restrict__ dq,
@@ -490,19 +490,13 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
                          const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
                          cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
-  {
-    const int threads = 256;
-    const long long blocks = (rows * 16 + threads - 1) / threads;
-    delta_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        static_cast<const T*>(o), static_cast<const T*>(d_o), delta, rows, s.D);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
+  (void)d_o;
   BwdParams p;
   p.cosp = cosp;
   p.sinp = sinp;
   p.lse = lse;
-  p.delta = delta;
+  p.o = o;
+  p.delta_out = delta;
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
