@@ -50,7 +50,8 @@ enum frsa_status {
   FRSA_ERR_LAUNCH = 6,          /* a CUDA launch or tensor-map encode failed */
   FRSA_ERR_DEVICE_TIMEOUT = 7,  /* a kernel gave up on a bounded wait (see frsa_query_status) */
   FRSA_ERR_NO_DEVICE = 8,       /* the current device is not sm_100 */
-  FRSA_ERR_WORKSPACE = 9        /* the backward workspace is missing or too small */
+  FRSA_ERR_WORKSPACE = 9,       /* the backward workspace is missing or too small */
+  FRSA_ERR_SCRATCH_LIMIT = 10   /* B*H*N*D exceeds frsa_bwd_noalloc_max_elements() */
 };
 
 typedef struct frsa_attn_args {
@@ -96,6 +97,24 @@ int frsa_bwd(const frsa_attn_args* args, void* stream);
  * head fits one CTA and dQ is reduced on chip). No reference counterpart:
  * the reference's dQ kernel (fa_rope_full .py:708-1009) recomputes instead. */
 size_t frsa_bwd_workspace_bytes(const frsa_attn_args* args);
+
+/* Backward pass that allocates nothing, for callers that cannot call
+ * cudaMalloc: plugin hosts that only hand over input and output buffers,
+ * runtimes whose device memory is fully carved up in advance, or loops that
+ * must avoid cudaMalloc/cudaFree because those can synchronise the device.
+ * Same arguments and results as frsa_bwd, but `workspace` is ignored: the f32
+ * dQ accumulator lives in a fixed array inside the library (16 MiB per device,
+ * kept until the process exits), so B*H*N*D must not exceed
+ * frsa_bwd_noalloc_max_elements() (else FRSA_ERR_SCRATCH_LIMIT, nothing
+ * launched). The first call on a device looks up that array's address (make
+ * it before any stream capture). All calls on a device share the array: each
+ * clears what it uses, and calls that run concurrently on the GPU race, so
+ * order them on one stream. No counterpart in the reference. */
+int frsa_bwd_noalloc(const frsa_attn_args* args, void* stream);
+
+/* Largest B*H*N*D frsa_bwd_noalloc accepts (4 Mi elements). No counterpart in
+ * the reference. */
+size_t frsa_bwd_noalloc_max_elements(void);
 
 /* Message for an FRSA_ERR_* code (static storage). */
 const char* frsa_strerror(int code);

@@ -22,6 +22,8 @@ EXPORTED_SYMBOLS = (
     "frsa_query_status",
     "frsa_abi_version",
     "frsa_last_error_detail",
+    "frsa_bwd_noalloc",
+    "frsa_bwd_noalloc_max_elements",
 )
 
 
@@ -89,6 +91,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.frsa_strerror.restype = ctypes.c_char_p
     lib.frsa_query_status.argtypes = []
     lib.frsa_query_status.restype = ctypes.c_int
+    lib.frsa_bwd_noalloc.argtypes = [ctypes.POINTER(FrsaAttnArgs), ctypes.c_void_p]
+    lib.frsa_bwd_noalloc.restype = ctypes.c_int
+    lib.frsa_bwd_noalloc_max_elements.argtypes = []
+    lib.frsa_bwd_noalloc_max_elements.restype = ctypes.c_size_t
     lib.frsa_last_error_detail.argtypes = []
     lib.frsa_last_error_detail.restype = ctypes.c_char_p
     lib.frsa_abi_version.argtypes = []

@@ -131,6 +131,9 @@ const char* frsa_strerror(int code) {
     case FRSA_ERR_DEVICE_TIMEOUT: return "frsa: a kernel timed out on a bounded wait";
     case FRSA_ERR_NO_DEVICE: return "frsa: the current CUDA device is not sm_100";
     case FRSA_ERR_WORKSPACE: return "frsa: backward workspace missing or too small";
+    case FRSA_ERR_SCRATCH_LIMIT:
+      return "frsa: B*H*N*D exceeds the built-in scratch of frsa_bwd_noalloc "
+             "(see frsa_bwd_noalloc_max_elements)";
     default: return "frsa: unknown error";
   }
 }
@@ -204,3 +207,6 @@ int frsa_query_status(void) {
 }
 
 }  // extern "C"
+
+// The allocation-free backward entry point (uses the helpers above).
+#include "frsa_noalloc.cu"
