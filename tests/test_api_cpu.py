@@ -1,0 +1,129 @@
+"""Host-side contract tests that need no GPU: the reference's assertions and
+error types, the compute-dtype rule, and the C-ABI library's exports and
+argument validation (only calls that return before touching a device)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import fa_rope_full
+from triton_fused_rope_flash_attn_b200 import (CosSinTable, TritonAttention, _lib,
+                                               _sdpa_comp_dtype, sdpa_triton_fa_rope)
+from triton_fused_rope_flash_attn_b200.build import INCLUDE, build_library
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_library()
+    return _lib.load()
+
+
+def test_dropin_module_exports():
+    for name in ("build_axial_rope_pairs", "CosSinTable", "_sdpa_comp_dtype", "TritonAttention",
+                 "sdpa_triton_fa_rope"):
+        assert hasattr(fa_rope_full, name)
+
+
+def test_comp_dtype_rule():
+    x = torch.zeros(1, dtype=torch.float32)
+    assert _sdpa_comp_dtype(x) == torch.float32
+    assert _sdpa_comp_dtype(x.bfloat16()) == torch.bfloat16
+    assert _sdpa_comp_dtype(x.half()) == torch.float16
+    with pytest.raises(TypeError):
+        _sdpa_comp_dtype(x.double())
+
+
+@pytest.mark.parametrize("N,has_cls,msg", [
+    (196, True, "SEQ_LEN must be 1 + H_img*W_img when has_cls=True (got 196 vs 197)."),
+    (197, False, "SEQ_LEN must equal H_img*W_img when has_cls=False (got 197 vs 196)."),
+])
+def test_seq_len_assertions(N, has_cls, msg):
+    q = torch.zeros(1, 1, N, 64)
+    cs = CosSinTable(100.0, 14, 64, device="cpu")
+    with pytest.raises(AssertionError, match=re.escape(msg)):
+        TritonAttention.apply(q, q, q, cs, 14, has_cls)
+
+
+def test_head_dim_assertion():
+    q = torch.zeros(1, 1, 197, 62)
+    cs = CosSinTable(100.0, 14, 64, device="cpu")
+    with pytest.raises(AssertionError, match="HEAD_DIM must be divisible by 4"):
+        sdpa_triton_fa_rope(q, q, q, cs)
+
+
+def test_cpu_tensors_fail_loudly():
+    """No CPU fallback: CPU inputs raise instead of computing."""
+    q = torch.zeros(1, 1, 197, 64)
+    cs = CosSinTable(100.0, 14, 64, device="cpu")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sdpa_triton_fa_rope(q, q, q, cs)
+
+
+def test_header_symbols_exported(lib):
+    with open(os.path.join(INCLUDE, "frsa.h")) as f:
+        hdr = f.read()
+    declared = set(re.findall(r"^\w[\w\s\*]*?\b(frsa_\w+)\(", hdr, flags=re.M))
+    assert declared == set(_lib.EXPORTED_SYMBOLS)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.frsa_abi_version() == 1
+
+
+def test_strerror_covers_codes(lib):
+    for code in range(0, 11):
+        msg = lib.frsa_strerror(code).decode()
+        assert msg and "unknown" not in msg, code
+    assert "unknown" in lib.frsa_strerror(99).decode()
+
+
+def _args(**kw):
+    a = _lib.FrsaAttnArgs()
+    a.q = a.k = a.v = a.o = a.lse = 0x1000
+    a.cosp = a.sinp = 0x2000
+    a.B, a.H, a.N, a.D, a.n_pos, a.has_cls = 1, 1, 197, 64, 196, 1
+    a.io_dtype = a.compute_dtype = _lib.FRSA_DTYPE_BF16
+    a.scale = 0.125
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), 1),
+    (dict(D=60), 3),
+    (dict(D=136), 3),
+    (dict(N=198), 2),               # table has 196 rows, N - has_cls = 197
+    (dict(has_cls=2), 2),
+    (dict(B=0), 2),
+    (dict(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_BF16), 4),
+    (dict(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32), 4),
+    (dict(k=0x1008), 5),
+])
+def test_fwd_validation_before_device(lib, kw, code):
+    assert lib.frsa_fwd(ctypes.byref(_args(**kw)), None) == code
+
+
+def test_bwd_requires_gradients_and_workspace(lib):
+    a = _args()
+    assert lib.frsa_bwd(ctypes.byref(a), None) == 1              # no d_o / dq / dk / dv
+    big = _args(N=257, n_pos=256, d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == 1 * 1 * 257 * 64 * 4
+    assert lib.frsa_bwd(ctypes.byref(big), None) == 9            # workspace missing
+    small = _args(d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(small)) == 0
+
+
+def test_table_shape_checked_by_wrapper():
+    from triton_fused_rope_flash_attn_b200.attention import _check_tables
+    c = torch.zeros(196, 32)
+    _check_tables(c, c, 197, 64, True, c.device)
+    with pytest.raises(ValueError):
+        _check_tables(c, c, 198, 64, True, c.device)
+    with pytest.raises(ValueError):
+        _check_tables(c[:, :16], c[:, :16], 197, 64, True, c.device)
+    with pytest.raises(TypeError):
+        _check_tables(c.double(), c.double(), 197, 64, True, c.device)
