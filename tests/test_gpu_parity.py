@@ -3,7 +3,8 @@
 Inputs are seeded, quantised to the compute dtype, and the oracle is evaluated
 in float64 on exactly those quantised values with the same float32 tables.
 Bar: max abs error <= 3e-2 and mean abs error <= 1e-3 on O, dQ, dK, dV (bf16;
-for N < 16 the mean bound is replaced by a 1e-2 relative bound);
+for N < 16 the mean bound is max(1e-3, 2e-2 * mean|exact|): P and dS are O(1)
+there and their bf16 rounding dominates);
 LSE within 1e-2 abs. The ViT-H-like case (inputs x2.0, D=80) is checked by
 relative error instead, because rounding the exact outputs to bf16 alone
 exceeds the absolute mean bound there.
@@ -75,7 +76,8 @@ def test_fwd_bwd_parity(case):
         if N < 16:
             # Few keys: P and dS are O(1) and their bf16 rounding (which the
             # reference applies too, fa_rope_full .py:965) dominates the mean.
-            assert rel_err(got[name], ref[name]) <= 1e-2, f"{name}: rel err"
+            bound = max(MEAN_ABS_TOL, 2e-2 * float(np.abs(ref[name]).mean()))
+            assert mean <= bound, f"{name}: mean abs err {mean:.3e} > {bound:.3e}"
         else:
             assert mean <= mean_tol(ref[name], case[6]), f"{name}: mean abs err {mean:.3e}"
     mx, _ = err_stats(got["lse"], ref["lse"])

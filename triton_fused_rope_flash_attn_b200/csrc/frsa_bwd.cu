@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tmem_alloc(&sm.tmem_base, kTmemColsBwd);
     tmem_relinquish();
   }
+  FRSA_STAMP(31);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -242,50 +243,76 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int j = j0 + jj, ks = jj % KVS;
       const int kv0 = j * kTile;
       const bool kv_valid = (kv0 + r) < N;
-      mbar_wait(&sm.kv_full[ks], (jj / KVS) & 1, abort_flag);
-      rotate_row_smem<T, NCH>(&sm.k[ks][0][0], r, D, rope_pos(kv0 + r, N, prm.has_cls), prm.cosp,
-                              prm.sinp);
+      {
+        RopeRows<NCH> rope;
+        load_rope_rows<NCH>(rope, wq * 32, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        mbar_wait(&sm.kv_full[ks], (jj / KVS) & 1, abort_flag);
+        FRSA_STAMP(22 + jj);
+        apply_rope_rows<T, NCH>(&sm.k[ks][0][0], wq * 32, D, rope, lane);
+      }
       for (int i = 0; i < nqt; ++i) {
         const int q0 = i * kTile;
         const bool fresh = !(RESIDENT && jj > 0);
         const int qs = RESIDENT ? i : qi % QS;
         if (fresh) {
-          mbar_wait(&sm.q_full[qs], (qi / QS) & 1, abort_flag);
-          rotate_row_smem<T, NCH>(&sm.q[qs][0][0], r, D, rope_pos(q0 + r, N, prm.has_cls),
-                                  prm.cosp, prm.sinp);
           const bool qv = (q0 + r) < N;
           sm.lse2[qs][r] = qv ? prm.lse[head_row0 + q0 + r] * 1.4426950408889634f : 0.f;
-          float dl = 0.f;
-          if (qv) {
-            // Delta = sum_d O dO over this query row (dO from the swizzled tile).
-            const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const T*>(prm.o) +
-                                                               (head_row0 + q0 + r) * D);
+          const int D2 = D >> 1;
+          // O pairs of the warp's 32 query rows (lane p holds pair p), read
+          // before the tile wait so the load overlaps it.
+          uint32_t ow[NCH][32];
 #pragma unroll
-            for (int gg = 0; gg < 8 * NCH; ++gg) {
-              if (gg * 8 < D) {
-                const uint4 a = __ldg(orow + gg);
-                const uint4 b = *reinterpret_cast<const uint4*>(&sm.dO[qs][gg >> 3][0] +
-                                                                 sw128_off(r, gg & 7));
-                const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+          for (int h = 0; h < NCH; ++h)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
-                  dl = fmaf(x.x, y.x, dl);
-                  dl = fmaf(x.y, y.y, dl);
-                }
+            for (int u = 0; u < 32; ++u) {
+              const int tok = q0 + wq * 32 + u, pp = lane + 32 * h;
+              ow[h][u] = (tok < N && pp < D2)
+                             ? __ldg(reinterpret_cast<const uint32_t*>(
+                                         static_cast<const T*>(prm.o) + (head_row0 + tok) * D) +
+                                     pp)
+                             : 0u;
+            }
+          RopeRows<NCH> rope;
+          load_rope_rows<NCH>(rope, wq * 32, q0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+          mbar_wait(&sm.q_full[qs], (qi / QS) & 1, abort_flag);
+          apply_rope_rows<T, NCH>(&sm.q[qs][0][0], wq * 32, D, rope, lane);
+          // Delta = sum_d O dO per query row: lane p multiplies pair p of O by
+          // pair p of the (unrotated) dO tile, then a warp reduction.
+          const uint32_t dob = smem_u32(&sm.dO[qs][0][0]);
+          float dl[32];
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            dl[u] = 0.f;
+#pragma unroll
+            for (int h = 0; h < NCH; ++h) {
+              const int pp = lane + 32 * h;
+              if (pp < D2) {
+                const float2 x = Elt<T>::unpack(ow[h][u]);
+                const float2 y = Elt<T>::unpack(lds_u32(dob + sw128_pair_off(wq * 32 + u, pp)));
+                dl[u] = fmaf(x.x, y.x, fmaf(x.y, y.y, dl[u]));
               }
             }
-            if (prm.delta_out != nullptr && j0 == 0 && jj == 0)
-              prm.delta_out[head_row0 + q0 + r] = dl;
           }
-          sm.delta[qs][r] = dl;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < 32; ++u) dl[u] += __shfl_xor_sync(0xffffffffu, dl[u], off);
+          // lane u keeps row wq*32+u's total
+          float mine = 0.f;
+#pragma unroll
+          for (int u = 0; u < 32; ++u) mine = (lane == u) ? dl[u] : mine;
+          sm.delta[qs][wq * 32 + lane] = mine;
+          if (prm.delta_out != nullptr && j0 == 0 && jj == 0 && q0 + wq * 32 + lane < N)
+            prm.delta_out[head_row0 + q0 + wq * 32 + lane] = mine;
           ++qi;
         }
         fence_proxy_async_smem();
         named_bar(1, 128);
         if (tid == 0) mbar_arrive(&sm.kq_ready);
+        if (it < 5) FRSA_STAMP(1 + it * 4 + 0);
 
         mbar_wait(&sm.st_full, it & 1, abort_flag);
+        if (it < 5) FRSA_STAMP(1 + it * 4 + 1);
         tc_fence_after();
         if (it > 0) mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);  // P/dS tiles free
         const int nqv = N - q0;  // valid query columns in this tile (may exceed 128)
@@ -327,28 +354,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (tid == 0) {
           mbar_arrive(&sm.ds_full);
           if (RESIDENT) mbar_arrive(&sm.tm_free);
+          if (it < 5) FRSA_STAMP(1 + it * 4 + 2);
         }
         if (!RESIDENT) {
           // dQ^ partial of this (key tile, query tile): scale and add into the workspace.
           mbar_wait(&sm.mm_done, it & 1, abort_flag);
           tc_fence_after();
-          const int qrow = q0 + r;
+          uint8_t* stage = &sm.p[0][0];  // P/dS tiles are free until the next iteration
 #pragma unroll 1
-          for (int c16 = 0; c16 < 8; ++c16) {
+          for (int c16 = 0; c16 < 4 * NCH; ++c16) {
             if (c16 * 16 < DP) {
               float v[16];
               tmem_ld16(tDPT + lane_off + c16 * 16, v);
               tmem_wait_ld();
-              if (qrow < N) {
-                float4* dst = reinterpret_cast<float4*>(prm.dq_accum + (head_row0 + qrow) * D +
-                                                        c16 * 16);
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                  if (c16 * 16 + g * 4 < D)
-                    atomicAdd(dst + g, make_float4(v[4 * g] * prm.scale, v[4 * g + 1] * prm.scale,
-                                                   v[4 * g + 2] * prm.scale,
-                                                   v[4 * g + 3] * prm.scale));
-                }
+              stage_write16<NCH>(stage, r, c16, v);
+            }
+          }
+          named_bar(1, 128);
+          {
+            const int D2 = D >> 1;
+#pragma unroll 2
+            for (int rr = wq * 32; rr < wq * 32 + 32; ++rr) {
+              const int tok = q0 + rr;
+              if (tok >= N) continue;
+              float2* dst = reinterpret_cast<float2*>(prm.dq_accum + (head_row0 + tok) * D);
+              for (int pp = lane; pp < D2; pp += 32) {
+                const float2 g = *reinterpret_cast<const float2*>(
+                    stage + stage_off<NCH>(rr, pp >> 1) + ((pp & 1) << 3));
+                atomicAdd(dst + pp, make_float2(g.x * prm.scale, g.y * prm.scale));
               }
             }
           }
@@ -359,66 +392,75 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ++it;
       }
       // dV, dK epilogue of key tile j
+      RopeRows<NCH> rope_k;
+      load_rope_rows<NCH>(rope_k, wq * 32, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
       mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
+      FRSA_STAMP(24 + jj);
       tc_fence_after();
       {
-        float acc[64 * NCH];
-#pragma unroll
+        // TMEM rows -> f32 staging (P/dS tiles, free now) -> warp-per-row drain.
+        uint8_t* stage_v = &sm.p[0][0];
+        uint8_t* stage_k = (NCH == 1) ? &sm.ds[0][0] : &sm.p[0][0];
+        T* dv_head = reinterpret_cast<T*>(prm.dv) + head_row0 * D;
+        T* dk_head = reinterpret_cast<T*>(prm.dk) + head_row0 * D;
+#pragma unroll 1
         for (int c16 = 0; c16 < 4 * NCH; ++c16) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tDV + lane_off + c16 * 16, v);
             tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e];
+            stage_write16<NCH>(stage_v, r, c16, v);
           }
         }
-        if (kv_valid)
-          store_row<T, 64 * NCH>(reinterpret_cast<T*>(prm.dv) + (head_row0 + kv0 + r) * D, acc, D);
-#pragma unroll
+        if (NCH != 1) {
+          named_bar(1, 128);
+          drain_rows_warp<T, NCH>(stage_v, wq * 32, kv0, N, D, 1.f, nullptr, dv_head, lane);
+          named_bar(1, 128);
+        }
+#pragma unroll 1
         for (int c16 = 0; c16 < 4 * NCH; ++c16) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tDK + lane_off + c16 * 16, v);
             tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e] * prm.scale;
+            stage_write16<NCH>(stage_k, r, c16, v);
           }
         }
-        if (kv_valid) {
-          unrotate_row_regs<64 * NCH>(acc, D, rope_pos(kv0 + r, N, prm.has_cls), prm.cosp,
-                                      prm.sinp);
-          store_row<T, 64 * NCH>(reinterpret_cast<T*>(prm.dk) + (head_row0 + kv0 + r) * D, acc, D);
-        }
+        named_bar(1, 128);
+        if (NCH == 1) drain_rows_warp<T, NCH>(stage_v, wq * 32, kv0, N, D, 1.f, nullptr, dv_head, lane);
+        drain_rows_warp<T, NCH>(stage_k, wq * 32, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
       }
       tc_fence_before();
       named_bar(1, 128);
       if (tid == 0) mbar_arrive(&sm.acc_free);
+      FRSA_STAMP(26 + jj);
     }
     if (RESIDENT) {
       // dQ epilogue: every MMA has completed (last mm_done waited above).
+      uint8_t* stage = &sm.p[0][0];
+      T* dq_head = reinterpret_cast<T*>(prm.dq) + head_row0 * D;
       for (int i = 0; i < nqt; ++i) {
-        const int qrow = i * kTile + r;
-        float acc[64];
-#pragma unroll
+        RopeRows<NCH> rope_q;
+        load_rope_rows<NCH>(rope_q, wq * 32, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
+                            lane);
+#pragma unroll 1
         for (int c16 = 0; c16 < 4; ++c16) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tmem + 384 + 64 * i + lane_off + c16 * 16, v);
             tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[c16 * 16 + e] = v[e] * prm.scale;
+            stage_write16<NCH>(stage, r, c16, v);
           }
         }
-        if (qrow < N) {
-          unrotate_row_regs<64>(acc, D, rope_pos(qrow, N, prm.has_cls), prm.cosp, prm.sinp);
-          store_row<T, 64>(reinterpret_cast<T*>(prm.dq) + (head_row0 + qrow) * D, acc, D);
-        }
+        named_bar(1, 128);
+        drain_rows_warp<T, NCH>(stage, wq * 32, i * kTile, N, D, prm.scale, &rope_q, dq_head,
+                                lane);
+        named_bar(1, 128);
       }
     }
   }
 
-  tc_fence_before();
+  FRSA_STAMP(30);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
     tmem_alloc(&sm.tmem_base, kTmemColsFwd);
     tmem_relinquish();
   }
+  FRSA_STAMP(31);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -157,19 +158,29 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
     float m2 = -INFINITY, l = 0.f;
 
     // Q rotation, then K_0 rotation.
-    mbar_wait(&sm.q_full, 0, abort_flag);
-    rotate_row_smem<T, NCH>(&sm.q[0][0], r, D, rope_pos(qrow, N, prm.has_cls), prm.cosp, prm.sinp);
-    mbar_wait(&sm.kv_full[0], 0, abort_flag);
-    rotate_row_smem<T, NCH>(&sm.k[0][0][0], r, D, rope_pos(r, N, prm.has_cls), prm.cosp, prm.sinp);
+    FRSA_STAMP(0);
+    {
+      RopeRows<NCH> rope;
+      load_rope_rows<NCH>(rope, wq * 32, q0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.q_full, 0, abort_flag);
+      FRSA_STAMP(1);
+      apply_rope_rows<T, NCH>(&sm.q[0][0], wq * 32, D, rope, lane);
+      load_rope_rows<NCH>(rope, wq * 32, 0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.kv_full[0], 0, abort_flag);
+      FRSA_STAMP(2);
+      apply_rope_rows<T, NCH>(&sm.k[0][0][0], wq * 32, D, rope, lane);
+    }
     fence_proxy_async_smem();
     named_bar(1, 128);
     if (tid == 0) mbar_arrive(&sm.k_ready[0]);
+    FRSA_STAMP(3);
 
     for (int j = 0; j < prm.nkv; ++j) {
       const int kv0 = j * kTile;
       const int nvalid = min(kTile, N - kv0);
       mbar_wait(&sm.s_full, j & 1, abort_flag);
       tc_fence_after();
+      FRSA_STAMP(4 + 5 * j);
 
       // pass 1: row max of the valid columns
       float mx = -INFINITY;
@@ -214,21 +225,26 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
       tc_fence_before();
       named_bar(1, 128);
       if (tid == 0) mbar_arrive(&sm.p_full);
+      FRSA_STAMP(5 + 5 * j);
 
       // rotate the next K tile while this tile's P V runs
       if (j + 1 < prm.nkv) {
         const int s1 = (j + 1) & 1;
+        RopeRows<NCH> rope;
+        load_rope_rows<NCH>(rope, wq * 32, kv0 + kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
+                            lane);
         mbar_wait(&sm.kv_full[s1], ((j + 1) >> 1) & 1, abort_flag);
-        rotate_row_smem<T, NCH>(&sm.k[s1][0][0], r, D, rope_pos(kv0 + kTile + r, N, prm.has_cls),
-                                prm.cosp, prm.sinp);
+        apply_rope_rows<T, NCH>(&sm.k[s1][0][0], wq * 32, D, rope, lane);
         fence_proxy_async_smem();
         named_bar(1, 128);
         if (tid == 0) mbar_arrive(&sm.k_ready[s1]);
       }
+      FRSA_STAMP(6 + 5 * j);
 
       // O = O * alpha + P V
       mbar_wait(&sm.o_full, j & 1, abort_flag);
       tc_fence_after();
+      FRSA_STAMP(7 + 5 * j);
 #pragma unroll
       for (int c16 = 0; c16 < 4 * NCH; ++c16) {
         if (c16 * 16 < DP) {
@@ -242,15 +258,26 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
       tc_fence_before();
     }
 
-    // epilogue: O / l and lse = (m + log2 l) ln 2
-    if (qrow < N) {
-      const float inv_l = 1.f / l;
-#pragma unroll
-      for (int i = 0; i < 64 * NCH; ++i) o_acc[i] *= inv_l;
-      T* orow = reinterpret_cast<T*>(prm.o) + (static_cast<size_t>(bh) * N + qrow) * D;
-      store_row<T, 64 * NCH>(orow, o_acc, D);
+    // epilogue: O / l and lse = (m + log2 l) ln 2. Rows go through an f32
+    // staging tile (the K stages, idle once the last P V has completed) and
+    // are written by warp-per-row coalesced stores.
+    const float inv_l = 1.f / l;
+    if (qrow < N)
       prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
+    uint8_t* stage = &sm.k[0][0][0];
+#pragma unroll
+    for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+      if (c16 * 16 < DP) {
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = o_acc[c16 * 16 + e] * inv_l;
+        stage_write16<NCH>(stage, r, c16, v);
+      }
     }
+    named_bar(1, 128);
+    drain_rows_warp<T, NCH>(stage, wq * 32, q0, N, D, 1.f, nullptr,
+                            reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D, lane);
+    FRSA_STAMP(30);
   }
 
   tc_fence_before();

@@ -48,6 +48,24 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// ---------------------------------------------------------------- tracing
+// Trace builds (-DFRSA_TRACE) record %globaltimer at phase boundaries of the
+// first 4096 CTAs, from thread 64 (first thread of the row warpgroup), into
+// g_trace[cta * 32 + slot]; frsa_trace_copy reads them back. Normal builds
+// compile the stamps away.
+#ifdef FRSA_TRACE
+__device__ unsigned long long g_trace[4096 * 32];
+#define FRSA_STAMP(slot)                                                       \
+  do {                                                                         \
+    if (blockIdx.x < 4096 && threadIdx.x == 64)                                \
+      ::frsa::g_trace[blockIdx.x * 32 + (slot)] = ::frsa::globaltimer();      \
+  } while (0)
+#else
+#define FRSA_STAMP(slot) \
+  do {                   \
+  } while (0)
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -233,6 +251,31 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- shared-space access
+// Explicit shared-state-space loads and stores. Unlike generic pointer
+// accesses, the compiler knows these cannot alias global memory, so global
+// loads around them keep their freedom to be hoisted and batched. They carry
+// no memory clobber, so ordinary global loads may still move across them, but
+// they are volatile: they stay ordered after the mbarrier waits and named
+// barriers (also volatile asm) that make the shared data valid.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v));
+}
+__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w));
 }
 
 // ---------------------------------------------------------------- math

@@ -22,6 +22,24 @@ __device__ __forceinline__ int rope_pos(int t, int N, int has_cls) {
   return t - has_cls;
 }
 
+// Pull the table rows of token position `pos` toward L1 ahead of use, so the
+// rotation that follows a TMA wait does not pay an L2 round trip per granule.
+__device__ __forceinline__ void prefetch_rope_row(int pos, int D, const float* __restrict__ cosp,
+                                                  const float* __restrict__ sinp) {
+  if (pos < 0) return;
+  const int D2 = D >> 1;
+  const char* c = reinterpret_cast<const char*>(cosp + static_cast<size_t>(pos) * D2);
+  const char* s = reinterpret_cast<const char*>(sinp + static_cast<size_t>(pos) * D2);
+  for (int off = 0; off < D2 * 4; off += 128) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(c + off));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(s + off));
+  }
+}
+
+// Rotate row r of a tile in place. Granules are processed four at a time with
+// every shared and table load of the group issued before any store, so the
+// loads overlap (the stores go through a generic pointer the compiler must
+// assume may alias the tables).
 template <typename T, int NCH>
 __device__ __forceinline__ void rotate_row_smem(uint8_t* tile, int r, int D, int pos,
                                                 const float* __restrict__ cosp,
@@ -32,20 +50,35 @@ __device__ __forceinline__ void rotate_row_smem(uint8_t* tile, int r, int D, int
   const float4* srow = reinterpret_cast<const float4*>(sinp + static_cast<size_t>(pos) * D2);
   const int ngran = D >> 3;  // 8 elements = 4 pairs per granule
 #pragma unroll
-  for (int gg = 0; gg < 8 * NCH; ++gg) {
-    if (gg < ngran) {
-      const int c = gg >> 3, g = gg & 7;
-      uint4* p = reinterpret_cast<uint4*>(tile + c * 16384 + sw128_off(r, g));
-      uint4 w = *p;
-      const float4 cs = __ldg(crow + gg);
-      const float4 sn = __ldg(srow + gg);
-      float2 a = Elt<T>::unpack(w.x), b = Elt<T>::unpack(w.y), cc = Elt<T>::unpack(w.z),
-             d = Elt<T>::unpack(w.w);
-      w.x = Elt<T>::pack(a.x * cs.x - a.y * sn.x, a.y * cs.x + a.x * sn.x);
-      w.y = Elt<T>::pack(b.x * cs.y - b.y * sn.y, b.y * cs.y + b.x * sn.y);
-      w.z = Elt<T>::pack(cc.x * cs.z - cc.y * sn.z, cc.y * cs.z + cc.x * sn.z);
-      w.w = Elt<T>::pack(d.x * cs.w - d.y * sn.w, d.y * cs.w + d.x * sn.w);
-      *p = w;
+  for (int g0 = 0; g0 < 8 * NCH; g0 += 4) {
+    if (g0 < ngran) {
+      uint4 w[4];
+      float4 cs[4], sn[4];
+      uint4* ptr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int gg = g0 + u;
+        ptr[u] = reinterpret_cast<uint4*>(tile + (gg >> 3) * 16384 + sw128_off(r, gg & 7));
+        if (gg < ngran) {
+          w[u] = *ptr[u];
+          cs[u] = __ldg(crow + gg);
+          sn[u] = __ldg(srow + gg);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (g0 + u < ngran) {
+          const float2 a = Elt<T>::unpack(w[u].x), b = Elt<T>::unpack(w[u].y),
+                       cc = Elt<T>::unpack(w[u].z), d = Elt<T>::unpack(w[u].w);
+          const float4 c = cs[u], s = sn[u];
+          uint4 o;
+          o.x = Elt<T>::pack(a.x * c.x - a.y * s.x, a.y * c.x + a.x * s.x);
+          o.y = Elt<T>::pack(b.x * c.y - b.y * s.y, b.y * c.y + b.x * s.y);
+          o.z = Elt<T>::pack(cc.x * c.z - cc.y * s.z, cc.y * c.z + cc.x * s.z);
+          o.w = Elt<T>::pack(d.x * c.w - d.y * s.w, d.y * c.w + d.x * s.w);
+          *ptr[u] = o;
+        }
+      }
     }
   }
 }
@@ -83,6 +116,128 @@ __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], int D) {
       w.z = Elt<T>::pack(v[8 * g + 4], v[8 * g + 5]);
       w.w = Elt<T>::pack(v[8 * g + 6], v[8 * g + 7]);
       reinterpret_cast<uint4*>(dst)[g] = w;
+    }
+  }
+}
+
+}  // namespace frsa
+
+namespace frsa {
+
+// ---------------------------------------------------------------------------
+// Warp-per-row helpers. A warp walks rows [r_begin, r_end) of a tile; lane p
+// owns RoPE pair p (columns 2p, 2p+1), so table reads are coalesced (one
+// 128-byte line per row for D = 64) and shared-memory accesses of a row hit 32
+// distinct banks.
+
+// Byte offset of pair p of row r in a 128B-swizzled chunked tile.
+__device__ __forceinline__ uint32_t sw128_pair_off(uint32_t r, uint32_t p) {
+  const uint32_t c = p >> 5, q = p & 31;
+  return c * 16384u + r * 128u + ((((q >> 2) ^ (r & 7u))) << 4) + ((q & 3u) << 2);
+}
+
+// Table values for the 32 rows a warp rotates, lane p holding pair p
+// (D <= 64) or pairs p and p + 32 (D <= 128). Loaded before the tile's TMA
+// wait so the table latency overlaps the load.
+template <int NCH>
+struct RopeRows {
+  float c[NCH][32], s[NCH][32];
+};
+
+template <int NCH>
+__device__ __forceinline__ void load_rope_rows(RopeRows<NCH>& t, int r_begin, int tok0, int N,
+                                               int has_cls, int D,
+                                               const float* __restrict__ cosp,
+                                               const float* __restrict__ sinp, int lane) {
+  const int D2 = D >> 1;
+#pragma unroll
+  for (int h = 0; h < NCH; ++h) {
+    const int p = lane + 32 * h;
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const int pos = rope_pos(tok0 + r_begin + u, N, has_cls);
+      t.c[h][u] = 1.f;
+      t.s[h][u] = 0.f;
+      if (pos >= 0 && p < D2) {
+        t.c[h][u] = __ldg(cosp + static_cast<size_t>(pos) * D2 + p);
+        t.s[h][u] = __ldg(sinp + static_cast<size_t>(pos) * D2 + p);
+      }
+    }
+  }
+}
+
+// Rotate the warp's 32 rows [r_begin, r_begin + 32) of a tile in place with
+// preloaded table values (rows that are not rotated carry c = 1, s = 0).
+template <typename T, int NCH>
+__device__ __forceinline__ void apply_rope_rows(uint8_t* tile, int r_begin, int D,
+                                                const RopeRows<NCH>& t, int lane) {
+  const int D2 = D >> 1;
+  const uint32_t base = smem_u32(tile);
+#pragma unroll
+  for (int h = 0; h < NCH; ++h) {
+    const int p = lane + 32 * h;
+    if (p < D2) {
+      uint32_t w[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) w[u] = lds_u32(base + sw128_pair_off(r_begin + u, p));
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float2 x = Elt<T>::unpack(w[u]);
+        const float c = t.c[h][u], s = t.s[h][u];
+        sts_u32(base + sw128_pair_off(r_begin + u, p),
+                Elt<T>::pack(x.x * c - x.y * s, x.y * c + x.x * s));
+      }
+    }
+  }
+}
+
+// Row stride and swizzle of the f32 staging tile used by the epilogues:
+// rows of 64*NCH floats, 16-byte chunk c of row r stored at chunk c ^ (r & 7).
+template <int NCH>
+__device__ __forceinline__ uint32_t stage_off(uint32_t r, uint32_t chunk) {
+  return r * (256u * NCH) + ((chunk ^ (r & 7u)) << 4);
+}
+
+// Thread-per-row write of 16 consecutive f32 values (columns 16*c16 ..) of row r.
+template <int NCH>
+__device__ __forceinline__ void stage_write16(uint8_t* stage, int r, int c16, const float (&v)[16]) {
+  const uint32_t base = smem_u32(stage);
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    sts_f4(base + stage_off<NCH>(r, c16 * 4 + u),
+           make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]));
+}
+
+// Warp-per-row drain of the warp's 32 staged f32 rows [r_begin, r_begin + 32):
+// scale, optional R^T un-rotation with preloaded tables (pass rope = nullptr
+// for none), rounding to T and a coalesced store to dst + tok * D for the rows
+// whose token tok0 + r is < N.
+template <typename T, int NCH>
+__device__ __forceinline__ void drain_rows_warp(const uint8_t* stage, int r_begin, int tok0, int N,
+                                                int D, float scale, const RopeRows<NCH>* rope,
+                                                T* dst, int lane) {
+  const int D2 = D >> 1;
+  const uint32_t base = smem_u32(stage);
+#pragma unroll
+  for (int h = 0; h < NCH; ++h) {
+    const int p = lane + 32 * h;
+    if (p < D2) {
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int r = r_begin + u;
+        const int tok = tok0 + r;
+        if (tok < N) {
+          const float2 g = lds_f2(base + stage_off<NCH>(r, p >> 1) + ((p & 1) << 3));
+          float e = g.x * scale, o = g.y * scale;
+          if (rope != nullptr) {
+            const float c = rope->c[h][u], s = rope->s[h][u];
+            const float e2 = e * c + o * s;
+            o = o * c - e * s;
+            e = e2;
+          }
+          reinterpret_cast<uint32_t*>(dst + static_cast<size_t>(tok) * D)[p] = Elt<T>::pack(e, o);
+        }
+      }
     }
   }
 }
