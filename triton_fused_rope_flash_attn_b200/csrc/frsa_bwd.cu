@@ -40,7 +40,9 @@ namespace frsa {
 
 namespace {
 
-constexpr int kBwdThreads = 192;
+constexpr int kComputeThreads = 256;                 // two warpgroups
+constexpr int kBwdThreads = 64 + kComputeThreads;    // + producer warp + MMA warp
+constexpr int kRowsPerWarp = kTile / (kComputeThreads / 32);  // 16
 constexpr uint32_t kTmemColsBwd = 512;
 
 template <int NCH>
@@ -231,138 +233,193 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ row warpgroup
-    const int wq = warp & 3;
+    // ------------------------------------------------------------ compute warps
+    // Two warpgroups (warps 2..9). For TMEM reads a thread owns row r (its
+    // lane quarter wq); warpgroup g takes S/dP columns [64g, 64g + 64) and
+    // every other 16-column block of the epilogue tiles. Warp-per-row phases
+    // (rotation, Delta, drains) give each of the 8 warps 16 rows.
+    constexpr int RW = kRowsPerWarp;
+    const int cw = warp - 2;                       // compute warp 0..7
+    const int g = cw >> 2;                         // warpgroup 0..1
+    const int wq = warp & 3;                       // TMEM lane quarter
     const int r = wq * 32 + lane;
+    const int rw0 = cw * RW;                       // first row of this warp's row slice
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const int tid = threadIdx.x - 64;
+    const bool leader = threadIdx.x == 64;
     const float c2 = prm.c2;
+    const int D2 = D >> 1;
     const size_t head_row0 = static_cast<size_t>(bh) * N;
-    int it = 0, qi = 0;
-    for (int jj = 0; jj < nj; ++jj) {
-      const int j = j0 + jj, ks = jj % KVS;
-      const int kv0 = j * kTile;
-      const bool kv_valid = (kv0 + r) < N;
-      {
-        RopeRows<NCH> rope;
-        load_rope_rows<NCH>(rope, wq * 32, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-        mbar_wait(&sm.kv_full[ks], (jj / KVS) & 1, abort_flag);
-        FRSA_STAMP(22 + jj);
-        apply_rope_rows<T, NCH>(&sm.k[ks][0][0], wq * 32, D, rope, lane);
+
+    // Rotate key tile jj_ of this CTA in its stage.
+    auto prep_k = [&](int jj_) {
+      RopeRows<NCH, RW> rope;
+      const int kv0_ = (j0 + jj_) * kTile;
+      load_rope_rows<NCH, RW>(rope, rw0, kv0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.kv_full[jj_ % KVS], (jj_ / KVS) & 1, abort_flag);
+      FRSA_STAMP(22 + (jj_ & 1));
+      apply_rope_rows<T, NCH, RW>(&sm.k[jj_ % KVS][0][0], rw0, D, rope, lane);
+    };
+    // Prepare query tile i_ in stage qs_ (the qi_-th query load): lse2 (+inf
+    // for padded rows, so their P is exactly 0), rotation of Q, and Delta.
+    auto prep_q = [&](int i_, int qs_, int qi_) {
+      const int q0_ = i_ * kTile;
+      if (g == 0) {
+        const bool qv = (q0_ + r) < N;
+        sm.lse2[qs_][r] = qv ? prm.lse[head_row0 + q0_ + r] * 1.4426950408889634f : INFINITY;
       }
+      // O pairs of this warp's query rows (lane p holds pair p), read before
+      // the tile wait so the load overlaps it.
+      uint32_t ow[NCH][RW];
+#pragma unroll
+      for (int h = 0; h < NCH; ++h)
+#pragma unroll
+        for (int u = 0; u < RW; ++u) {
+          const int tok = q0_ + rw0 + u, pp = lane + 32 * h;
+          ow[h][u] = (tok < N && pp < D2)
+                         ? __ldg(reinterpret_cast<const uint32_t*>(
+                                     static_cast<const T*>(prm.o) + (head_row0 + tok) * D) +
+                                 pp)
+                         : 0u;
+        }
+      RopeRows<NCH, RW> rope;
+      load_rope_rows<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
+      apply_rope_rows<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      // Delta = sum_d O dO per query row: lane p multiplies pair p of O by pair
+      // p of the (unrotated) dO tile, then a warp reduction.
+      const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
+      float dl[RW];
+#pragma unroll
+      for (int u = 0; u < RW; ++u) {
+        dl[u] = 0.f;
+#pragma unroll
+        for (int h = 0; h < NCH; ++h) {
+          const int pp = lane + 32 * h;
+          if (pp < D2) {
+            const float2 x = Elt<T>::unpack(ow[h][u]);
+            const float2 y = Elt<T>::unpack(lds_u32(dob + sw128_pair_off(rw0 + u, pp)));
+            dl[u] = fmaf(x.x, y.x, fmaf(x.y, y.y, dl[u]));
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int u = 0; u < RW; ++u) dl[u] += __shfl_xor_sync(0xffffffffu, dl[u], off);
+      if (lane < RW) {
+        float mine = 0.f;
+#pragma unroll
+        for (int u = 0; u < RW; ++u) mine = (lane == u) ? dl[u] : mine;
+        sm.delta[qs_][rw0 + lane] = mine;
+        if (prm.delta_out != nullptr && j0 == 0 && q0_ + rw0 + lane < N)
+          prm.delta_out[head_row0 + q0_ + rw0 + lane] = mine;
+      }
+    };
+
+    // First iteration's operands, then one iteration of look-ahead: the next
+    // key/query tile is prepared while the tensor core computes S^T and dP^T.
+    int it = 0, qi = 0;
+    prep_k(0);
+    prep_q(0, 0, 0);
+    qi = 1;
+    int cur_qs = 0;
+    fence_proxy_async_smem();
+    named_bar(1, kComputeThreads);
+    if (leader) mbar_arrive(&sm.kq_ready);
+    for (int jj = 0; jj < nj; ++jj) {
+      const int j = j0 + jj;
+      const int kv0 = j * kTile;
       for (int i = 0; i < nqt; ++i) {
         const int q0 = i * kTile;
-        const bool fresh = !(RESIDENT && jj > 0);
-        const int qs = RESIDENT ? i : qi % QS;
-        if (fresh) {
-          const bool qv = (q0 + r) < N;
-          sm.lse2[qs][r] = qv ? prm.lse[head_row0 + q0 + r] * 1.4426950408889634f : 0.f;
-          const int D2 = D >> 1;
-          // O pairs of the warp's 32 query rows (lane p holds pair p), read
-          // before the tile wait so the load overlaps it.
-          uint32_t ow[NCH][32];
-#pragma unroll
-          for (int h = 0; h < NCH; ++h)
-#pragma unroll
-            for (int u = 0; u < 32; ++u) {
-              const int tok = q0 + wq * 32 + u, pp = lane + 32 * h;
-              ow[h][u] = (tok < N && pp < D2)
-                             ? __ldg(reinterpret_cast<const uint32_t*>(
-                                         static_cast<const T*>(prm.o) + (head_row0 + tok) * D) +
-                                     pp)
-                             : 0u;
-            }
-          RopeRows<NCH> rope;
-          load_rope_rows<NCH>(rope, wq * 32, q0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-          mbar_wait(&sm.q_full[qs], (qi / QS) & 1, abort_flag);
-          apply_rope_rows<T, NCH>(&sm.q[qs][0][0], wq * 32, D, rope, lane);
-          // Delta = sum_d O dO per query row: lane p multiplies pair p of O by
-          // pair p of the (unrotated) dO tile, then a warp reduction.
-          const uint32_t dob = smem_u32(&sm.dO[qs][0][0]);
-          float dl[32];
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            dl[u] = 0.f;
-#pragma unroll
-            for (int h = 0; h < NCH; ++h) {
-              const int pp = lane + 32 * h;
-              if (pp < D2) {
-                const float2 x = Elt<T>::unpack(ow[h][u]);
-                const float2 y = Elt<T>::unpack(lds_u32(dob + sw128_pair_off(wq * 32 + u, pp)));
-                dl[u] = fmaf(x.x, y.x, fmaf(x.y, y.y, dl[u]));
-              }
-            }
+        const int qs = cur_qs;
+        const bool has_next = (i + 1 < nqt) || (jj + 1 < nj);
+        // Look-ahead needs the next query tile in a different stage: with one
+        // stage it can only arrive after this iteration's MMAs, so it is
+        // prepared after them instead (prep_late).
+        auto prep_next = [&]() {
+          const int nj_ = (i + 1 < nqt) ? jj : jj + 1;
+          const int ni = (i + 1 < nqt) ? i + 1 : 0;
+          if (ni == 0) prep_k(nj_);
+          const bool nfresh = !(RESIDENT && nj_ > 0);
+          const int nqs = RESIDENT ? ni : qi % QS;
+          if (nfresh) {
+            prep_q(ni, nqs, qi);
+            ++qi;
           }
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int u = 0; u < 32; ++u) dl[u] += __shfl_xor_sync(0xffffffffu, dl[u], off);
-          // lane u keeps row wq*32+u's total
-          float mine = 0.f;
-#pragma unroll
-          for (int u = 0; u < 32; ++u) mine = (lane == u) ? dl[u] : mine;
-          sm.delta[qs][wq * 32 + lane] = mine;
-          if (prm.delta_out != nullptr && j0 == 0 && jj == 0 && q0 + wq * 32 + lane < N)
-            prm.delta_out[head_row0 + q0 + wq * 32 + lane] = mine;
-          ++qi;
-        }
-        fence_proxy_async_smem();
-        named_bar(1, 128);
-        if (tid == 0) mbar_arrive(&sm.kq_ready);
+          cur_qs = nqs;
+        };
+        const bool prep_late = has_next && (QS == 1 || KVS == 1);
+        if (has_next && !prep_late) prep_next();
         if (it < 5) FRSA_STAMP(1 + it * 4 + 0);
 
         mbar_wait(&sm.st_full, it & 1, abort_flag);
         if (it < 5) FRSA_STAMP(1 + it * 4 + 1);
         tc_fence_after();
         if (it > 0) mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);  // P/dS tiles free
-        const int nqv = N - q0;  // valid query columns in this tile (may exceed 128)
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          float sv[32], dp[32];
-          tmem_ld32(tST + lane_off + cc * 32, sv);
-          tmem_ld32(tDPT + lane_off + cc * 32, dp);
+        {
+          // This warpgroup's 64 columns: S^T and dP^T loaded at once. Padded
+          // query columns have lse2 = +inf (P = 0, dS = 0); padded key rows
+          // only reach dV/dK rows that are never stored and dQ through zero
+          // K^ rows, so no per-element masking is needed.
+          float sv[2][32], dp[2][32];
+          tmem_ld32(tST + lane_off + g * 64, sv[0]);
+          tmem_ld32(tST + lane_off + g * 64 + 32, sv[1]);
+          tmem_ld32(tDPT + lane_off + g * 64, dp[0]);
+          tmem_ld32(tDPT + lane_off + g * 64 + 32, dp[1]);
           tmem_wait_ld();
+          const uint32_t pbase = smem_u32(sm.p[g]), dbase = smem_u32(sm.ds[g]);
+          const uint32_t lbase = smem_u32(&sm.lse2[qs][g * 64]);
+          const uint32_t ebase = smem_u32(&sm.delta[qs][g * 64]);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int qc = cc * 32 + c;
-            const float pv =
-                (kv_valid && qc < nqv) ? ex2(fmaf(sv[c], c2, -sm.lse2[qs][qc])) : 0.f;
-            sv[c] = pv;
-            dp[c] = pv * (dp[c] - sm.delta[qs][qc]);
-          }
-          uint8_t* pch = sm.p[cc >> 1];
-          uint8_t* dch = sm.ds[cc >> 1];
+          for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            const uint32_t off = sw128_off(r, (cc & 1) * 4 + g4);
-            uint4 w;
-            w.x = Elt<T>::pack(sv[g4 * 8 + 0], sv[g4 * 8 + 1]);
-            w.y = Elt<T>::pack(sv[g4 * 8 + 2], sv[g4 * 8 + 3]);
-            w.z = Elt<T>::pack(sv[g4 * 8 + 4], sv[g4 * 8 + 5]);
-            w.w = Elt<T>::pack(sv[g4 * 8 + 6], sv[g4 * 8 + 7]);
-            *reinterpret_cast<uint4*>(pch + off) = w;
-            w.x = Elt<T>::pack(dp[g4 * 8 + 0], dp[g4 * 8 + 1]);
-            w.y = Elt<T>::pack(dp[g4 * 8 + 2], dp[g4 * 8 + 3]);
-            w.z = Elt<T>::pack(dp[g4 * 8 + 4], dp[g4 * 8 + 5]);
-            w.w = Elt<T>::pack(dp[g4 * 8 + 6], dp[g4 * 8 + 7]);
-            *reinterpret_cast<uint4*>(dch + off) = w;
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 l4 = lds_f4(lbase + (hh * 32 + c4 * 4) * 4);
+              const float4 d4 = lds_f4(ebase + (hh * 32 + c4 * 4) * 4);
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c = c4 * 4 + e;
+                const float pv = ex2(fmaf(sv[hh][c], c2, -lv[e]));
+                sv[hh][c] = pv;
+                dp[hh][c] = pv * (dp[hh][c] - dv4[e]);
+              }
+            }
+#pragma unroll
+            for (int g4 = 0; g4 < 4; ++g4) {
+              const uint32_t off = sw128_off(r, hh * 4 + g4);
+              uint4 w;
+              w.x = Elt<T>::pack(sv[hh][g4 * 8 + 0], sv[hh][g4 * 8 + 1]);
+              w.y = Elt<T>::pack(sv[hh][g4 * 8 + 2], sv[hh][g4 * 8 + 3]);
+              w.z = Elt<T>::pack(sv[hh][g4 * 8 + 4], sv[hh][g4 * 8 + 5]);
+              w.w = Elt<T>::pack(sv[hh][g4 * 8 + 6], sv[hh][g4 * 8 + 7]);
+              sts_u4(pbase + off, w);
+              w.x = Elt<T>::pack(dp[hh][g4 * 8 + 0], dp[hh][g4 * 8 + 1]);
+              w.y = Elt<T>::pack(dp[hh][g4 * 8 + 2], dp[hh][g4 * 8 + 3]);
+              w.z = Elt<T>::pack(dp[hh][g4 * 8 + 4], dp[hh][g4 * 8 + 5]);
+              w.w = Elt<T>::pack(dp[hh][g4 * 8 + 6], dp[hh][g4 * 8 + 7]);
+              sts_u4(dbase + off, w);
+            }
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        named_bar(1, 128);
-        if (tid == 0) {
+        named_bar(1, kComputeThreads);
+        if (leader) {
           mbar_arrive(&sm.ds_full);
-          if (RESIDENT) mbar_arrive(&sm.tm_free);
-          if (it < 5) FRSA_STAMP(1 + it * 4 + 2);
+          if (RESIDENT) {
+            mbar_arrive(&sm.tm_free);
+            if (has_next && !prep_late) mbar_arrive(&sm.kq_ready);
+          }
         }
+        if (it < 5) FRSA_STAMP(1 + it * 4 + 2);
         if (!RESIDENT) {
           // dQ^ partial of this (key tile, query tile): scale and add into the workspace.
           mbar_wait(&sm.mm_done, it & 1, abort_flag);
           tc_fence_after();
           uint8_t* stage = &sm.p[0][0];  // P/dS tiles are free until the next iteration
 #pragma unroll 1
-          for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+          for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
             if (c16 * 16 < DP) {
               float v[16];
               tmem_ld16(tDPT + lane_off + c16 * 16, v);
@@ -370,30 +427,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               stage_write16<NCH>(stage, r, c16, v);
             }
           }
-          named_bar(1, 128);
+          named_bar(1, kComputeThreads);
           {
-            const int D2 = D >> 1;
-#pragma unroll 2
-            for (int rr = wq * 32; rr < wq * 32 + 32; ++rr) {
-              const int tok = q0 + rr;
+            const uint32_t sbase = smem_u32(stage);
+#pragma unroll 4
+            for (int u = 0; u < RW; ++u) {
+              const int rr = rw0 + u, tok = q0 + rr;
               if (tok >= N) continue;
               float2* dst = reinterpret_cast<float2*>(prm.dq_accum + (head_row0 + tok) * D);
               for (int pp = lane; pp < D2; pp += 32) {
-                const float2 g = *reinterpret_cast<const float2*>(
-                    stage + stage_off<NCH>(rr, pp >> 1) + ((pp & 1) << 3));
-                atomicAdd(dst + pp, make_float2(g.x * prm.scale, g.y * prm.scale));
+                const float2 gv = lds_f2(sbase + stage_off<NCH>(rr, pp >> 1) + ((pp & 1) << 3));
+                atomicAdd(dst + pp, make_float2(gv.x * prm.scale, gv.y * prm.scale));
               }
             }
           }
           tc_fence_before();
-          named_bar(1, 128);
-          if (tid == 0) mbar_arrive(&sm.tm_free);
+          named_bar(1, kComputeThreads);
+          if (leader) {
+            mbar_arrive(&sm.tm_free);
+            if (has_next && !prep_late) mbar_arrive(&sm.kq_ready);
+          }
+        }
+        if (prep_late) {
+          prep_next();
+          fence_proxy_async_smem();
+          named_bar(1, kComputeThreads);
+          if (leader) mbar_arrive(&sm.kq_ready);
         }
         ++it;
       }
       // dV, dK epilogue of key tile j
-      RopeRows<NCH> rope_k;
-      load_rope_rows<NCH>(rope_k, wq * 32, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      RopeRows<NCH, RW> rope_k;
+      load_rope_rows<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
       mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
       FRSA_STAMP(24 + jj);
       tc_fence_after();
@@ -404,7 +469,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         T* dv_head = reinterpret_cast<T*>(prm.dv) + head_row0 * D;
         T* dk_head = reinterpret_cast<T*>(prm.dk) + head_row0 * D;
 #pragma unroll 1
-        for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+        for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tDV + lane_off + c16 * 16, v);
@@ -413,12 +478,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
         if (NCH != 1) {
-          named_bar(1, 128);
-          drain_rows_warp<T, NCH>(stage_v, wq * 32, kv0, N, D, 1.f, nullptr, dv_head, lane);
-          named_bar(1, 128);
+          named_bar(1, kComputeThreads);
+          drain_rows_warp<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, nullptr, dv_head, lane);
+          named_bar(1, kComputeThreads);
         }
 #pragma unroll 1
-        for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+        for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tDK + lane_off + c16 * 16, v);
@@ -426,13 +491,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             stage_write16<NCH>(stage_k, r, c16, v);
           }
         }
-        named_bar(1, 128);
-        if (NCH == 1) drain_rows_warp<T, NCH>(stage_v, wq * 32, kv0, N, D, 1.f, nullptr, dv_head, lane);
-        drain_rows_warp<T, NCH>(stage_k, wq * 32, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
+        named_bar(1, kComputeThreads);
+        if (NCH == 1)
+          drain_rows_warp<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, nullptr, dv_head, lane);
+        drain_rows_warp<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
       }
       tc_fence_before();
-      named_bar(1, 128);
-      if (tid == 0) mbar_arrive(&sm.acc_free);
+      named_bar(1, kComputeThreads);
+      if (leader) mbar_arrive(&sm.acc_free);
       FRSA_STAMP(26 + jj);
     }
     if (RESIDENT) {
@@ -440,11 +506,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint8_t* stage = &sm.p[0][0];
       T* dq_head = reinterpret_cast<T*>(prm.dq) + head_row0 * D;
       for (int i = 0; i < nqt; ++i) {
-        RopeRows<NCH> rope_q;
-        load_rope_rows<NCH>(rope_q, wq * 32, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
-                            lane);
+        RopeRows<NCH, RW> rope_q;
+        load_rope_rows<NCH, RW>(rope_q, rw0, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
+                                lane);
 #pragma unroll 1
-        for (int c16 = 0; c16 < 4; ++c16) {
+        for (int c16 = g; c16 < 4; c16 += 2) {
           if (c16 * 16 < DP) {
             float v[16];
             tmem_ld16(tmem + 384 + 64 * i + lane_off + c16 * 16, v);
@@ -452,10 +518,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             stage_write16<NCH>(stage, r, c16, v);
           }
         }
-        named_bar(1, 128);
-        drain_rows_warp<T, NCH>(stage, wq * 32, i * kTile, N, D, prm.scale, &rope_q, dq_head,
-                                lane);
-        named_bar(1, 128);
+        named_bar(1, kComputeThreads);
+        drain_rows_warp<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &rope_q, dq_head,
+                                    lane);
+        named_bar(1, kComputeThreads);
       }
     }
   }

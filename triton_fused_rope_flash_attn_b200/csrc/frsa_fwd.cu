@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
       }
     }
     named_bar(1, 128);
-    drain_rows_warp<T, NCH>(stage, wq * 32, q0, N, D, 1.f, nullptr,
+    drain_rows_warp<T, NCH, 32>(stage, wq * 32, q0, N, D, 1.f, nullptr,
                             reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D, lane);
     FRSA_STAMP(30);
   }

@@ -139,13 +139,13 @@ __device__ __forceinline__ uint32_t sw128_pair_off(uint32_t r, uint32_t p) {
 // Table values for the 32 rows a warp rotates, lane p holding pair p
 // (D <= 64) or pairs p and p + 32 (D <= 128). Loaded before the tile's TMA
 // wait so the table latency overlaps the load.
-template <int NCH>
+template <int NCH, int ROWS = 32>
 struct RopeRows {
-  float c[NCH][32], s[NCH][32];
+  float c[NCH][ROWS], s[NCH][ROWS];
 };
 
-template <int NCH>
-__device__ __forceinline__ void load_rope_rows(RopeRows<NCH>& t, int r_begin, int tok0, int N,
+template <int NCH, int ROWS = 32>
+__device__ __forceinline__ void load_rope_rows(RopeRows<NCH, ROWS>& t, int r_begin, int tok0, int N,
                                                int has_cls, int D,
                                                const float* __restrict__ cosp,
                                                const float* __restrict__ sinp, int lane) {
@@ -154,7 +154,7 @@ __device__ __forceinline__ void load_rope_rows(RopeRows<NCH>& t, int r_begin, in
   for (int h = 0; h < NCH; ++h) {
     const int p = lane + 32 * h;
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
+    for (int u = 0; u < ROWS; ++u) {
       const int pos = rope_pos(tok0 + r_begin + u, N, has_cls);
       t.c[h][u] = 1.f;
       t.s[h][u] = 0.f;
@@ -166,22 +166,22 @@ __device__ __forceinline__ void load_rope_rows(RopeRows<NCH>& t, int r_begin, in
   }
 }
 
-// Rotate the warp's 32 rows [r_begin, r_begin + 32) of a tile in place with
-// preloaded table values (rows that are not rotated carry c = 1, s = 0).
-template <typename T, int NCH>
+// Rotate the warp's ROWS rows [r_begin, r_begin + ROWS) of a tile in place
+// with preloaded table values (rows that are not rotated carry c = 1, s = 0).
+template <typename T, int NCH, int ROWS = 32>
 __device__ __forceinline__ void apply_rope_rows(uint8_t* tile, int r_begin, int D,
-                                                const RopeRows<NCH>& t, int lane) {
+                                                const RopeRows<NCH, ROWS>& t, int lane) {
   const int D2 = D >> 1;
   const uint32_t base = smem_u32(tile);
 #pragma unroll
   for (int h = 0; h < NCH; ++h) {
     const int p = lane + 32 * h;
     if (p < D2) {
-      uint32_t w[32];
+      uint32_t w[ROWS];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) w[u] = lds_u32(base + sw128_pair_off(r_begin + u, p));
+      for (int u = 0; u < ROWS; ++u) w[u] = lds_u32(base + sw128_pair_off(r_begin + u, p));
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < ROWS; ++u) {
         const float2 x = Elt<T>::unpack(w[u]);
         const float c = t.c[h][u], s = t.s[h][u];
         sts_u32(base + sw128_pair_off(r_begin + u, p),
@@ -208,14 +208,15 @@ __device__ __forceinline__ void stage_write16(uint8_t* stage, int r, int c16, co
            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]));
 }
 
-// Warp-per-row drain of the warp's 32 staged f32 rows [r_begin, r_begin + 32):
+// Warp-per-row drain of the warp's ROWS staged f32 rows [r_begin, r_begin + ROWS):
 // scale, optional R^T un-rotation with preloaded tables (pass rope = nullptr
 // for none), rounding to T and a coalesced store to dst + tok * D for the rows
 // whose token tok0 + r is < N.
-template <typename T, int NCH>
+template <typename T, int NCH, int ROWS = 32>
 __device__ __forceinline__ void drain_rows_warp(const uint8_t* stage, int r_begin, int tok0, int N,
-                                                int D, float scale, const RopeRows<NCH>* rope,
-                                                T* dst, int lane) {
+                                                int D, float scale,
+                                                const RopeRows<NCH, ROWS>* rope, T* dst,
+                                                int lane) {
   const int D2 = D >> 1;
   const uint32_t base = smem_u32(stage);
 #pragma unroll
@@ -223,7 +224,7 @@ __device__ __forceinline__ void drain_rows_warp(const uint8_t* stage, int r_begi
     const int p = lane + 32 * h;
     if (p < D2) {
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < ROWS; ++u) {
         const int r = r_begin + u;
         const int tok = tok0 + r;
         if (tok < N) {
