@@ -14,6 +14,7 @@
 
 #include "frsa_bwd.cu"
 #include "frsa_fwd.cu"
+#include "frsa_fwd_small.cu"
 
 namespace {
 

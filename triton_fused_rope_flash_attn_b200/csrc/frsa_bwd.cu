@@ -252,12 +252,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
     // Rotate key tile jj_ of this CTA in its stage.
     auto prep_k = [&](int jj_) {
-      RopeRows<NCH, RW> rope;
+      RopeQ<NCH, RW> rope;
       const int kv0_ = (j0 + jj_) * kTile;
-      load_rope_rows<NCH, RW>(rope, rw0, kv0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      load_rope_q<NCH, RW>(rope, rw0, kv0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
       mbar_wait(&sm.kv_full[jj_ % KVS], (jj_ / KVS) & 1, abort_flag);
       FRSA_STAMP(22 + (jj_ & 1));
-      apply_rope_rows<T, NCH, RW>(&sm.k[jj_ % KVS][0][0], rw0, D, rope, lane);
+      apply_rope_q<T, NCH, RW>(&sm.k[jj_ % KVS][0][0], rw0, D, rope, lane);
     };
     // Prepare query tile i_ in stage qs_ (the qi_-th query load): lse2 (+inf
     // for padded rows, so their P is exactly 0), rotation of Q, and Delta.
@@ -267,52 +267,52 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const bool qv = (q0_ + r) < N;
         sm.lse2[qs_][r] = qv ? prm.lse[head_row0 + q0_ + r] * 1.4426950408889634f : INFINITY;
       }
-      // O pairs of this warp's query rows (lane p holds pair p), read before
-      // the tile wait so the load overlaps it.
-      uint32_t ow[NCH][RW];
+      // O granules of this warp's query rows (quad layout), read before the
+      // tile wait so the load overlaps it.
+      const int rq = lane >> 3, gl = lane & 7;
+      uint4 og[NCH][RW / 4];
 #pragma unroll
-      for (int h = 0; h < NCH; ++h)
-#pragma unroll
-        for (int u = 0; u < RW; ++u) {
-          const int tok = q0_ + rw0 + u, pp = lane + 32 * h;
-          ow[h][u] = (tok < N && pp < D2)
-                         ? __ldg(reinterpret_cast<const uint32_t*>(
-                                     static_cast<const T*>(prm.o) + (head_row0 + tok) * D) +
-                                 pp)
-                         : 0u;
-        }
-      RopeRows<NCH, RW> rope;
-      load_rope_rows<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
-      apply_rope_rows<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
-      // Delta = sum_d O dO per query row: lane p multiplies pair p of O by pair
-      // p of the (unrotated) dO tile, then a warp reduction.
-      const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
-      float dl[RW];
-#pragma unroll
-      for (int u = 0; u < RW; ++u) {
-        dl[u] = 0.f;
+      for (int k = 0; k < RW / 4; ++k)
 #pragma unroll
         for (int h = 0; h < NCH; ++h) {
-          const int pp = lane + 32 * h;
-          if (pp < D2) {
-            const float2 x = Elt<T>::unpack(ow[h][u]);
-            const float2 y = Elt<T>::unpack(lds_u32(dob + sw128_pair_off(rw0 + u, pp)));
-            dl[u] = fmaf(x.x, y.x, fmaf(x.y, y.y, dl[u]));
+          const int tok = q0_ + rw0 + 4 * k + rq, gg = gl + 8 * h;
+          og[h][k] = (tok < N && 8 * gg < D)
+                         ? __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(prm.o) +
+                                                                (head_row0 + tok) * D) + gg)
+                         : make_uint4(0u, 0u, 0u, 0u);
+        }
+      RopeQ<NCH, RW> rope;
+      load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
+      apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      // Delta = sum_d O dO per query row: each lane dots its granule of O with
+      // the same granule of the (unrotated) dO tile; 8 lanes share a row.
+      const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
+#pragma unroll
+      for (int k = 0; k < RW / 4; ++k) {
+        float dl = 0.f;
+#pragma unroll
+        for (int h = 0; h < NCH; ++h) {
+          if (8 * (gl + 8 * h) < D) {
+            const uint4 b = lds_u4(dob + h * 16384 + sw128_off(rw0 + 4 * k + rq, gl));
+            const uint32_t aw[4] = {og[h][k].x, og[h][k].y, og[h][k].z, og[h][k].w};
+            const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
+              dl = fmaf(x.x, y.x, fmaf(x.y, y.y, dl));
+            }
           }
         }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-        for (int u = 0; u < RW; ++u) dl[u] += __shfl_xor_sync(0xffffffffu, dl[u], off);
-      if (lane < RW) {
-        float mine = 0.f;
-#pragma unroll
-        for (int u = 0; u < RW; ++u) mine = (lane == u) ? dl[u] : mine;
-        sm.delta[qs_][rw0 + lane] = mine;
-        if (prm.delta_out != nullptr && j0 == 0 && q0_ + rw0 + lane < N)
-          prm.delta_out[head_row0 + q0_ + rw0 + lane] = mine;
+        dl += __shfl_xor_sync(0xffffffffu, dl, 1);
+        dl += __shfl_xor_sync(0xffffffffu, dl, 2);
+        dl += __shfl_xor_sync(0xffffffffu, dl, 4);
+        if (gl == 0) {
+          const int rr = rw0 + 4 * k + rq;
+          sm.delta[qs_][rr] = dl;
+          if (prm.delta_out != nullptr && j0 == 0 && q0_ + rr < N)
+            prm.delta_out[head_row0 + q0_ + rr] = dl;
+        }
       }
     };
 
@@ -430,14 +430,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           named_bar(1, kComputeThreads);
           {
             const uint32_t sbase = smem_u32(stage);
-#pragma unroll 4
-            for (int u = 0; u < RW; ++u) {
-              const int rr = rw0 + u, tok = q0 + rr;
-              if (tok >= N) continue;
-              float2* dst = reinterpret_cast<float2*>(prm.dq_accum + (head_row0 + tok) * D);
-              for (int pp = lane; pp < D2; pp += 32) {
-                const float2 gv = lds_f2(sbase + stage_off<NCH>(rr, pp >> 1) + ((pp & 1) << 3));
-                atomicAdd(dst + pp, make_float2(gv.x * prm.scale, gv.y * prm.scale));
+            const int rq = lane >> 3, gl = lane & 7;
+#pragma unroll
+            for (int k = 0; k < RW / 4; ++k) {
+              const int rr = rw0 + 4 * k + rq, tok = q0 + rr;
+#pragma unroll
+              for (int h = 0; h < NCH; ++h) {
+                const int gg = gl + 8 * h;
+                if (tok < N && 8 * gg < D) {
+                  float v[8];
+                  stage_read8<NCH>(sbase, rr, gg, prm.scale, v);
+                  float4* dst = reinterpret_cast<float4*>(prm.dq_accum + (head_row0 + tok) * D + 8 * gg);
+                  atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
+                  atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], v[7]));
+                }
               }
             }
           }
@@ -457,8 +463,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ++it;
       }
       // dV, dK epilogue of key tile j
-      RopeRows<NCH, RW> rope_k;
-      load_rope_rows<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      RopeQ<NCH, RW> rope_k;
+      load_rope_q<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
       mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
       FRSA_STAMP(24 + jj);
       tc_fence_after();
@@ -479,7 +485,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         if (NCH != 1) {
           named_bar(1, kComputeThreads);
-          drain_rows_warp<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, nullptr, dv_head, lane);
+          drain_q<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, static_cast<const RopeQ<NCH, RW>*>(nullptr), dv_head, lane);
           named_bar(1, kComputeThreads);
         }
 #pragma unroll 1
@@ -493,8 +499,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         named_bar(1, kComputeThreads);
         if (NCH == 1)
-          drain_rows_warp<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, nullptr, dv_head, lane);
-        drain_rows_warp<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
+          drain_q<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, static_cast<const RopeQ<NCH, RW>*>(nullptr), dv_head, lane);
+        drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
       }
       tc_fence_before();
       named_bar(1, kComputeThreads);
@@ -506,8 +512,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint8_t* stage = &sm.p[0][0];
       T* dq_head = reinterpret_cast<T*>(prm.dq) + head_row0 * D;
       for (int i = 0; i < nqt; ++i) {
-        RopeRows<NCH, RW> rope_q;
-        load_rope_rows<NCH, RW>(rope_q, rw0, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
+        RopeQ<NCH, RW> rope_q;
+        load_rope_q<NCH, RW>(rope_q, rw0, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
                                 lane);
 #pragma unroll 1
         for (int c16 = g; c16 < 4; c16 += 2) {
@@ -519,7 +525,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
         named_bar(1, kComputeThreads);
-        drain_rows_warp<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &rope_q, dq_head,
+        drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &rope_q, dq_head,
                                     lane);
         named_bar(1, kComputeThreads);
       }

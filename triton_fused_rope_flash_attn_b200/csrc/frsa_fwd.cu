@@ -1,41 +1,56 @@
 // Forward kernel: O = softmax(R(Q) R(K)^T * scale) V with 2D RoPE fused.
 //
 // Restates the computation of _attn_fwd (fa_rope_full .py:91-315) as a
-// warp-specialised tcgen05 kernel. One CTA owns one (batch*head, 128-query tile)
-// unit and walks the keys in 128-key tiles with an online softmax in base 2.
+// warp-specialised tcgen05 kernel. One CTA owns a pair of 128-query tiles of
+// one (batch*head) (the whole head when N <= 256) and walks the keys in
+// 128-key tiles with an online softmax in base 2. The two query tiles share
+// every K/V load and K rotation.
 //
-//   warp 0      TMA producer: Q tile once, then K/V tiles into a 2-stage ring
+//   warp 0      TMA producer: the two Q tiles once, then K/V tiles into a
+//               ring of KS stages
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  "row" warpgroup: rotates Q and each K tile in shared memory,
-//               reads S from TMEM (thread = query row), writes P (16-bit) to
-//               shared memory, accumulates O in registers from the per-tile
-//               P V product, and writes O and the log-sum-exp.
+//   warps 2..3  rotation warps: apply RoPE in shared memory to the Q tiles and
+//               to every K tile as soon as TMA has landed it
+//   warps 4..11 two compute warpgroups, warpgroup g owns query tile g of the
+//               pair: it reads S from TMEM (thread = query row), writes P
+//               (16-bit) to its own shared tile, accumulates O in registers
+//               from the per-tile P V product, and writes O and the
+//               log-sum-exp. The MMA issue order (P_0 V, S_0 next, P_1 V,
+//               S_1 next) lets the two groups run out of phase, so one's
+//               softmax overlaps the other's MMAs.
 //
-// TMEM columns: [0,128) S tile (f32), [128, 128+DP) per-tile P V (f32).
+// TMEM columns: warpgroup g uses [256 g, 256 g + 128) for S and
+// [256 g + 128, 256 g + 128 + DP) for the per-tile P V.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
+
+#undef FRSA_STAMP_TID
+#define FRSA_STAMP_TID 128  // first compute thread of this kernel
 
 namespace frsa {
 
 namespace {
 
-constexpr int kFwdThreads = 192;
-constexpr uint32_t kTmemColsFwd = 256;
+constexpr int kFwdCompute = 256;                // two warpgroups
+constexpr int kFwdThreads = 128 + kFwdCompute;  // + producer, MMA and two rotation warps
+constexpr uint32_t kTmemColsFwd = 512;
 
 template <int NCH>
 struct FwdSmem {
-  uint8_t q[NCH][kChunkBytes];
-  uint8_t k[2][NCH][kChunkBytes];
-  uint8_t v[2][NCH][kChunkBytes];
-  uint8_t p[2][kChunkBytes];  // P tile [128 q][128 kv], two 64-column K chunks
-  uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
-  uint64_t k_ready[2];
-  uint64_t s_full;
-  uint64_t p_full;
-  uint64_t o_full;
+  static constexpr int KS = (NCH == 1) ? 2 : 1;  // K/V ring stages
+  uint8_t q[2][NCH][kChunkBytes];      // query tile of warpgroup g
+  uint8_t k[KS][NCH][kChunkBytes];     // key ring
+  uint8_t v[KS][NCH][kChunkBytes];     // value ring
+  uint8_t p[2][2][kChunkBytes];        // P tile of warpgroup g: [128 q][128 kv], two chunks
+  uint64_t q_full[2];
+  uint64_t q_ready;
+  uint64_t kv_full[KS];
+  uint64_t kv_empty[KS];
+  uint64_t k_ready[KS];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -45,41 +60,45 @@ struct FwdParams {
   const float* sinp;
   void* o;
   float* lse;
-  int N, D, nqt, nkv, has_cls;
+  int N, D, nqt, npair, nkv, has_cls;
   float c2;  // scale * log2(e)
 };
 
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
+  using Sm = FwdSmem<NCH>;
+  constexpr int KS = Sm::KS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  FwdSmem<NCH>* smp = aligned_smem<FwdSmem<NCH>>(smem_raw);
+  Sm* smp = aligned_smem<Sm>(smem_raw);
   if (smp == nullptr) return;
-  FwdSmem<NCH>& sm = *smp;
+  Sm& sm = *smp;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int unit = blockIdx.x;
-  const int bh = unit / prm.nqt;
-  const int qt = unit - bh * prm.nqt;
-  const int q0 = qt * kTile;
+  const int bh = blockIdx.x / prm.npair;
+  const int pr = blockIdx.x - bh * prm.npair;
   const int N = prm.N, D = prm.D;
   const int DP = (D + 15) & ~15;   // MMA N for P V
   const int ksteps = DP >> 4;      // MMA K steps over the head dim
+  const int nact = min(2, prm.nqt - 2 * pr);  // active query tiles in this pair (1 or 2)
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
-    mbar_init(&sm.q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.p_full[s], 1);
+      mbar_init(&sm.o_full[s], 1);
+    }
+    mbar_init(&sm.q_ready, 1);
+    for (int s = 0; s < KS; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
       mbar_init(&sm.k_ready[s], 1);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.p_full, 1);
-    mbar_init(&sm.o_full, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -91,8 +110,6 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tS = tmem;
-  const uint32_t tO = tmem + kTile;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -100,11 +117,14 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&sm.q_full, NCH * kChunkBytes);
-      for (int c = 0; c < NCH; ++c) tma_load_3d(sm.q[c], &tm_q, &sm.q_full, c * kChunkCols, q0, bh);
+      for (int g = 0; g < nact; ++g) {
+        mbar_arrive_expect_tx(&sm.q_full[g], NCH * kChunkBytes);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sm.q[g][c], &tm_q, &sm.q_full[g], c * kChunkCols, (2 * pr + g) * kTile, bh);
+      }
       for (int j = 0; j < prm.nkv; ++j) {
-        const int s = j & 1;
-        mbar_wait(&sm.kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag);
+        const int s = j % KS;
+        mbar_wait(&sm.kv_empty[s], ((j / KS) & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.kv_full[s], 2 * NCH * kChunkBytes);
         for (int c = 0; c < NCH; ++c) {
           tma_load_3d(sm.k[s][c], &tm_k, &sm.kv_full[s], c * kChunkCols, j * kTile, bh);
@@ -118,166 +138,234 @@ __global__ void __launch_bounds__(kFwdThreads, (NCH == 1 ? 2 : 1))
       constexpr bool kBf = Elt<T>::kBf16;
       const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);
       const uint32_t idO = idesc_f16(kBf, 128, DP, false, true);
-      for (int j = 0; j < prm.nkv; ++j) {
-        const int s = j & 1;
-        mbar_wait(&sm.k_ready[s], (j >> 1) & 1, abort_flag);
-        tc_fence_after();
-        // S = Q^ K^T : A = Q^ [q][d] K-major, B = K^ [kv][d] K-major.
+      // S_g = Q^_g K^T : A = Q^ [q][d] K-major, B = K^ [kv][d] K-major.
+      auto issue_s = [&](int g, int j) {
+        const int s = j % KS;
+        const uint32_t tS = tmem + 256 * g;
         for (int ks = 0; ks < ksteps; ++ks) {
           const int c = ks >> 2;
           const uint32_t koff = (ks & 3) * 32;
-          const uint64_t a = sw128_desc(smem_u32(sm.q[c]) + koff, 16, 1024);
-          const uint64_t b = sw128_desc(smem_u32(sm.k[s][c]) + koff, 16, 1024);
-          mma_ss(tS, a, b, idS, ks > 0);
+          mma_ss(tS, sw128_desc(smem_u32(sm.q[g][c]) + koff, 16, 1024),
+                 sw128_desc(smem_u32(sm.k[s][c]) + koff, 16, 1024), idS, ks > 0);
         }
-        mma_commit(&sm.s_full);
-        mbar_wait(&sm.p_full, j & 1, abort_flag);
-        tc_fence_after();
-        // O_j = P V : A = P [q][kv] K-major, B = V [kv][d] MN-major.
+        mma_commit(&sm.s_full[g]);
+      };
+      // O_g = P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major.
+      auto issue_pv = [&](int g, int j) {
+        const int s = j % KS;
+        const uint32_t tO = tmem + 256 * g + 128;
         for (int ks = 0; ks < kTile / 16; ++ks) {
-          const uint64_t a = sw128_desc(smem_u32(sm.p[ks >> 2]) + (ks & 3) * 32, 16, 1024);
-          const uint64_t b = sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024);
-          mma_ss(tO, a, b, idO, ks > 0);
+          mma_ss(tO, sw128_desc(smem_u32(sm.p[g][ks >> 2]) + (ks & 3) * 32, 16, 1024),
+                 sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024), idO, ks > 0);
         }
-        mma_commit(&sm.o_full);
-        mma_commit(&sm.kv_empty[s]);
+        mma_commit(&sm.o_full[g]);
+      };
+      mbar_wait(&sm.q_ready, 0, abort_flag);
+      mbar_wait(&sm.k_ready[0], 0, abort_flag);
+      tc_fence_after();
+      for (int g = 0; g < nact; ++g) issue_s(g, 0);
+      for (int j = 0; j < prm.nkv; ++j) {
+        const bool more = j + 1 < prm.nkv;
+        if (KS == 1) {
+          // One K/V stage: tile j+1 can only land after every P V of tile j.
+          for (int g = 0; g < nact; ++g) {
+            mbar_wait(&sm.p_full[g], j & 1, abort_flag);
+            tc_fence_after();
+            issue_pv(g, j);
+          }
+          mma_commit(&sm.kv_empty[0]);
+          if (more) {
+            mbar_wait(&sm.k_ready[0], (j + 1) & 1, abort_flag);
+            tc_fence_after();
+            for (int g = 0; g < nact; ++g) issue_s(g, j + 1);
+          }
+        } else {
+          for (int g = 0; g < nact; ++g) {
+            mbar_wait(&sm.p_full[g], j & 1, abort_flag);
+            tc_fence_after();
+            issue_pv(g, j);
+            if (more) {
+              if (g == 0) {
+                mbar_wait(&sm.k_ready[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag);
+                tc_fence_after();
+              }
+              issue_s(g, j + 1);
+            }
+          }
+          mma_commit(&sm.kv_empty[j % KS]);
+        }
       }
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ rotation warps
+    // 64 threads; each warp rotates half of every tile, 16 rows at a time with
+    // the table values loaded before the tile's TMA wait.
+    const int rwp = warp - 2;
+    auto rotate_tile = [&](uint8_t* tile, int tok0, uint64_t* full, uint32_t parity) {
+#pragma unroll 1
+      for (int blk = 0; blk < 4; ++blk) {
+        const int r0 = rwp * 64 + blk * 16;
+        RopeQ<NCH, 16> rope;
+        load_rope_q<NCH, 16>(rope, r0, tok0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        if (blk == 0) mbar_wait(full, parity, abort_flag);
+        apply_rope_q<T, NCH, 16>(tile, r0, D, rope, lane);
+      }
+    };
+    for (int g = 0; g < nact; ++g)
+      rotate_tile(&sm.q[g][0][0], (2 * pr + g) * kTile, &sm.q_full[g], 0);
+    fence_proxy_async_smem();
+    named_bar(1, 64);
+    if (threadIdx.x == 64) mbar_arrive(&sm.q_ready);
+    for (int j = 0; j < prm.nkv; ++j) {
+      const int s = j % KS;
+      rotate_tile(&sm.k[s][0][0], j * kTile, &sm.kv_full[s], (j / KS) & 1);
+      fence_proxy_async_smem();
+      named_bar(1, 64);
+      if (threadIdx.x == 64) mbar_arrive(&sm.k_ready[s]);
     }
   } else {
-    // ------------------------------------------------------------ row warpgroup
-    const int wq = warp & 3;               // TMEM lane quarter this warp may access
-    const int r = wq * 32 + lane;          // tile row == TMEM lane
+    // ------------------------------------------------------------ compute warpgroups
+    const int cw = warp - 4;
+    const int g = cw >> 2;                 // warpgroup = query tile of the pair
+    const int wq = warp & 3;               // TMEM lane quarter
+    const int r = wq * 32 + lane;          // query row in the tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const int tid = threadIdx.x - 64;      // 0..127 inside the warpgroup
+    const bool leader = threadIdx.x == 128 + 128 * g;
+    const int q0 = (2 * pr + g) * kTile;
     const int qrow = q0 + r;
     const float c2 = prm.c2;
+    const uint32_t tS = tmem + 256 * g + lane_off;
+    const uint32_t tO = tmem + 256 * g + 128 + lane_off;
 
-    float o_acc[64 * NCH];
+    if (g < nact) {
+      float o_acc[64 * NCH];
 #pragma unroll
-    for (int i = 0; i < 64 * NCH; ++i) o_acc[i] = 0.f;
-    float m2 = -INFINITY, l = 0.f;
+      for (int i = 0; i < 64 * NCH; ++i) o_acc[i] = 0.f;
+      float m2 = -INFINITY, l = 0.f;
+      const bool row_valid = qrow < N;
+      // A warp whose 32 query rows are all padding skips the softmax math: its
+      // P rows only ever reach O rows that are not stored.
+      const bool warp_active = (q0 + wq * 32) < N;
 
-    // Q rotation, then K_0 rotation.
-    FRSA_STAMP(0);
-    {
-      RopeRows<NCH> rope;
-      load_rope_rows<NCH>(rope, wq * 32, q0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.q_full, 0, abort_flag);
-      FRSA_STAMP(1);
-      apply_rope_rows<T, NCH>(&sm.q[0][0], wq * 32, D, rope, lane);
-      load_rope_rows<NCH>(rope, wq * 32, 0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.kv_full[0], 0, abort_flag);
-      FRSA_STAMP(2);
-      apply_rope_rows<T, NCH>(&sm.k[0][0][0], wq * 32, D, rope, lane);
-    }
-    fence_proxy_async_smem();
-    named_bar(1, 128);
-    if (tid == 0) mbar_arrive(&sm.k_ready[0]);
-    FRSA_STAMP(3);
+      FRSA_STAMP(3);
 
-    for (int j = 0; j < prm.nkv; ++j) {
-      const int kv0 = j * kTile;
-      const int nvalid = min(kTile, N - kv0);
-      mbar_wait(&sm.s_full, j & 1, abort_flag);
-      tc_fence_after();
-      FRSA_STAMP(4 + 5 * j);
-
-      // pass 1: row max of the valid columns
-      float mx = -INFINITY;
+      for (int j = 0; j < prm.nkv; ++j) {
+        const int kv0 = j * kTile;
+        const int nvalid = min(kTile, N - kv0);
+        mbar_wait(&sm.s_full[g], j & 1, abort_flag);
+        tc_fence_after();
+        if (j == 0) FRSA_STAMP(4);
+        float alpha = 1.f;
+        if (warp_active) {
+          // pass 1: row max over the valid columns
+          float mx = -INFINITY;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float sv[32];
-        tmem_ld32(tS + lane_off + cc * 32, sv);
-        tmem_wait_ld();
+          for (int h = 0; h < 2; ++h) {
+            float sv[2][32];
+            tmem_ld32(tS + h * 64, sv[0]);
+            tmem_ld32(tS + h * 64 + 32, sv[1]);
+            tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (cc * 32 + i < nvalid) mx = fmaxf(mx, sv[i]);
-      }
-      const float m_new = fmaxf(m2, mx * c2);
-      const float alpha = ex2(m2 - m_new);
-      // pass 2: P = exp2(S c2 - m), row sum, 16-bit P into shared memory
-      float sum = 0.f;
+            for (int u = 0; u < 2; ++u)
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float sv[32];
-        tmem_ld32(tS + lane_off + cc * 32, sv);
-        tmem_wait_ld();
+              for (int i = 0; i < 32; ++i)
+                if (h * 64 + u * 32 + i < nvalid) mx = fmaxf(mx, sv[u][i]);
+          }
+          const float m_new = fmaxf(m2, mx * c2);
+          alpha = ex2(m2 - m_new);
+          // pass 2: P = exp2(S c2 - m), row sum, 16-bit P into this group's tile
+          float sum = 0.f;
+          const uint32_t pb0 = smem_u32(sm.p[g][0]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float pv = (cc * 32 + i < nvalid) ? ex2(fmaf(sv[i], c2, -m_new)) : 0.f;
-          sv[i] = pv;
-          sum += pv;
+          for (int h = 0; h < 2; ++h) {
+            float sv[2][32];
+            tmem_ld32(tS + h * 64, sv[0]);
+            tmem_ld32(tS + h * 64 + 32, sv[1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cbase = h * 64 + u * 32;
+              if (cbase + 32 <= nvalid) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  sv[u][i] = ex2(fmaf(sv[u][i], c2, -m_new));
+                  sum += sv[u][i];
+                }
+              } else if (cbase < nvalid) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  sv[u][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[u][i], c2, -m_new)) : 0.f;
+                  sum += sv[u][i];
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[u][i] = 0.f;
+              }
+#pragma unroll
+              for (int g4 = 0; g4 < 4; ++g4) {
+                uint4 w;
+                w.x = Elt<T>::pack(sv[u][g4 * 8 + 0], sv[u][g4 * 8 + 1]);
+                w.y = Elt<T>::pack(sv[u][g4 * 8 + 2], sv[u][g4 * 8 + 3]);
+                w.z = Elt<T>::pack(sv[u][g4 * 8 + 4], sv[u][g4 * 8 + 5]);
+                w.w = Elt<T>::pack(sv[u][g4 * 8 + 6], sv[u][g4 * 8 + 7]);
+                sts_u4(pb0 + h * kChunkBytes + sw128_off(r, u * 4 + g4), w);
+              }
+            }
+          }
+          l = l * alpha + sum;
+          m2 = m_new;
         }
-        uint8_t* pchunk = sm.p[cc >> 1];
-#pragma unroll
-        for (int g4 = 0; g4 < 4; ++g4) {
-          uint4 w;
-          w.x = Elt<T>::pack(sv[g4 * 8 + 0], sv[g4 * 8 + 1]);
-          w.y = Elt<T>::pack(sv[g4 * 8 + 2], sv[g4 * 8 + 3]);
-          w.z = Elt<T>::pack(sv[g4 * 8 + 4], sv[g4 * 8 + 5]);
-          w.w = Elt<T>::pack(sv[g4 * 8 + 6], sv[g4 * 8 + 7]);
-          *reinterpret_cast<uint4*>(pchunk + sw128_off(r, (cc & 1) * 4 + g4)) = w;
-        }
-      }
-      l = l * alpha + sum;
-      m2 = m_new;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      named_bar(1, 128);
-      if (tid == 0) mbar_arrive(&sm.p_full);
-      FRSA_STAMP(5 + 5 * j);
-
-      // rotate the next K tile while this tile's P V runs
-      if (j + 1 < prm.nkv) {
-        const int s1 = (j + 1) & 1;
-        RopeRows<NCH> rope;
-        load_rope_rows<NCH>(rope, wq * 32, kv0 + kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
-                            lane);
-        mbar_wait(&sm.kv_full[s1], ((j + 1) >> 1) & 1, abort_flag);
-        apply_rope_rows<T, NCH>(&sm.k[s1][0][0], wq * 32, D, rope, lane);
         fence_proxy_async_smem();
-        named_bar(1, 128);
-        if (tid == 0) mbar_arrive(&sm.k_ready[s1]);
-      }
-      FRSA_STAMP(6 + 5 * j);
+        tc_fence_before();
+        named_bar(2 + g, 128);
+        if (leader) mbar_arrive(&sm.p_full[g]);
+        if (j == 0) FRSA_STAMP(5);
 
-      // O = O * alpha + P V
-      mbar_wait(&sm.o_full, j & 1, abort_flag);
-      tc_fence_after();
-      FRSA_STAMP(7 + 5 * j);
+        // O = O * alpha + P V
+        mbar_wait(&sm.o_full[g], j & 1, abort_flag);
+        tc_fence_after();
+        if (warp_active) {
 #pragma unroll
-      for (int c16 = 0; c16 < 4 * NCH; ++c16) {
-        if (c16 * 16 < DP) {
-          float ov[16];
-          tmem_ld16(tO + lane_off + c16 * 16, ov);
-          tmem_wait_ld();
+          for (int c32 = 0; c32 < 2 * NCH; ++c32) {
+            if (c32 * 32 < DP) {
+              float ov[32];
+              tmem_ld32(tO + c32 * 32, ov);
+              tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o_acc[c16 * 16 + i] = fmaf(o_acc[c16 * 16 + i], alpha, ov[i]);
+              for (int i = 0; i < 32; ++i)
+                o_acc[c32 * 32 + i] = fmaf(o_acc[c32 * 32 + i], alpha, ov[i]);
+            }
+          }
+        }
+        tc_fence_before();
+      }
+      FRSA_STAMP(7);
+
+      // epilogue: lse = (m + log2 l) ln 2 and O / l, written through this
+      // group's P tile (free: the last P V has completed) as an f32 staging
+      // area, one 64-column block at a time, by warp-per-row coalesced stores.
+      if (row_valid)
+        prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
+      const float inv_l = warp_active ? 1.f / l : 0.f;
+      uint8_t* stage = &sm.p[g][0][0];
+      T* o_head = reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D;
+#pragma unroll
+      for (int blk = 0; blk < NCH; ++blk) {
+        if (blk * 64 < D) {
+#pragma unroll
+          for (int c16 = 0; c16 < 4; ++c16) {
+            float v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = o_acc[blk * 64 + c16 * 16 + e] * inv_l;
+            stage_write16<1>(stage, r, c16, v);
+          }
+          named_bar(2 + g, 128);
+          drain_block_q<T, 32>(stage, wq * 32, q0, N, D, blk, o_head, lane);
+          named_bar(2 + g, 128);
         }
       }
-      tc_fence_before();
+      FRSA_STAMP(30);
     }
-
-    // epilogue: O / l and lse = (m + log2 l) ln 2. Rows go through an f32
-    // staging tile (the K stages, idle once the last P V has completed) and
-    // are written by warp-per-row coalesced stores.
-    const float inv_l = 1.f / l;
-    if (qrow < N)
-      prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
-    uint8_t* stage = &sm.k[0][0][0];
-#pragma unroll
-    for (int c16 = 0; c16 < 4 * NCH; ++c16) {
-      if (c16 * 16 < DP) {
-        float v[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = o_acc[c16 * 16 + e] * inv_l;
-        stage_write16<NCH>(stage, r, c16, v);
-      }
-    }
-    named_bar(1, 128);
-    drain_rows_warp<T, NCH, 32>(stage, wq * 32, q0, N, D, 1.f, nullptr,
-                            reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D, lane);
-    FRSA_STAMP(30);
   }
 
   tc_fence_before();
@@ -300,17 +388,16 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
+  p.npair = (p.nqt + 1) / 2;
   p.nkv = p.nqt;
   p.has_cls = s.has_cls;
   p.c2 = s.scale * 1.4426950408889634f;
-  // The dynamic window starts 1024-aligned in practice; the slack covers a
-  // smaller alignment and keeps two NCH=1 CTAs within one SM's 228 KiB.
-  const size_t smem = sizeof(FwdSmem<NCH>) + 256;
+  const size_t smem = sizeof(FwdSmem<NCH>) + 1024;
   auto kern = fwd_kernel<T, NCH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const long long units = static_cast<long long>(s.BH) * p.nqt;
+  const long long units = static_cast<long long>(s.BH) * p.npair;
   kern<<<static_cast<unsigned>(units), kFwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, p);
   return cudaGetLastError();
 }
@@ -320,6 +407,7 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
 cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                        const CUtensorMap& tm_v, const float* cosp, const float* sinp, void* o,
                        float* lse, cudaStream_t stream) {
+  if (fwd_small_applies(s)) return launch_fwd_small(s, tm_q, tm_k, tm_v, cosp, sinp, o, lse, stream);
   const bool two = s.D > 64;
   if (s.bf16) {
     return two ? launch_fwd_t<__nv_bfloat16, 2>(s, tm_q, tm_k, tm_v, cosp, sinp, o, lse, stream)

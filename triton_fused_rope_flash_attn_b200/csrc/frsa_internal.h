@@ -26,6 +26,12 @@ cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUte
                        const CUtensorMap& tm_v, const float* cosp, const float* sinp, void* o,
                        float* lse, cudaStream_t stream);
 
+// Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
+bool fwd_small_applies(const LaunchShape& s);
+cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
+                             const CUtensorMap& tm_k, const CUtensorMap& tm_v, const float* cosp,
+                             const float* sinp, void* o, float* lse, cudaStream_t stream);
+
 // Backward (delta preprocess + main kernel + optional dQ finalize).
 // dq_accum: fp32 [BH, N, D] workspace or nullptr when bwd_needs_workspace() is false.
 bool bwd_needs_workspace(const LaunchShape& s);

@@ -50,19 +50,30 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 // ---------------------------------------------------------------- tracing
 // Trace builds (-DFRSA_TRACE) record %globaltimer at phase boundaries of the
-// first 4096 CTAs, from thread 64 (first thread of the row warpgroup), into
+// first 4096 CTAs, from thread FRSA_STAMP_TID (the first compute thread), into
 // g_trace[cta * 32 + slot]; frsa_trace_copy reads them back. Normal builds
 // compile the stamps away.
+#ifndef FRSA_STAMP_TID
+#define FRSA_STAMP_TID 64
+#endif
 #ifdef FRSA_TRACE
 __device__ unsigned long long g_trace[4096 * 32];
 #define FRSA_STAMP(slot)                                                       \
   do {                                                                         \
-    if (blockIdx.x < 4096 && threadIdx.x == 64)                                \
+    if (blockIdx.x < 4096 && threadIdx.x == FRSA_STAMP_TID)                    \
+      ::frsa::g_trace[blockIdx.x * 32 + (slot)] = ::frsa::globaltimer();      \
+  } while (0)
+#define FRSA_STAMP_T(slot, tid)                                                \
+  do {                                                                         \
+    if (blockIdx.x < 4096 && threadIdx.x == (tid))                             \
       ::frsa::g_trace[blockIdx.x * 32 + (slot)] = ::frsa::globaltimer();      \
   } while (0)
 #else
 #define FRSA_STAMP(slot) \
   do {                   \
+  } while (0)
+#define FRSA_STAMP_T(slot, tid) \
+  do {                          \
   } while (0)
 #endif
 
@@ -90,14 +101,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in hardware (woken when the phase completes, or after the hint of
+// ~0.1 ms) instead of spinning, so waiting warps do not steal issue slots from
+// the warps doing work on the same sub-partition.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(100000u)
       : "memory");
   return ok != 0;
 }
@@ -111,7 +126,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 255u) == 0u) {
+    if ((it & 7u) == 0u) {
       if (*abort_flag) return false;
       const uint64_t now = globaltimer();
       if (t0 == 0) {
@@ -270,6 +285,13 @@ __device__ __forceinline__ float2 lds_f2(uint32_t addr) {
   asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -301,31 +323,37 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
-// 16-bit element traits.
+// 16-bit element traits: pack two f32 into one 32-bit word (first value in
+// the low half) and back, in registers only.
 template <typename T>
 struct Elt;
 template <>
 struct Elt<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
   __device__ static __forceinline__ uint32_t pack(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+    uint32_t u;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(b), "f"(a));
+    return u;
   }
   __device__ static __forceinline__ float2 unpack(uint32_t w) {
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w);
-    return __bfloat1622float2(h);
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
   }
 };
 template <>
 struct Elt<__half> {
   static constexpr bool kBf16 = false;
   __device__ static __forceinline__ uint32_t pack(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+    uint32_t u;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(b), "f"(a));
+    return u;
   }
   __device__ static __forceinline__ float2 unpack(uint32_t w) {
-    __half2 h = *reinterpret_cast<__half2*>(&w);
-    return __half22float2(h);
+    float lo, hi;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "cvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(w));
+    return make_float2(lo, hi);
   }
 };
 

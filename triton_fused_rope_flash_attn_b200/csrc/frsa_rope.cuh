@@ -1,15 +1,24 @@
-// In-shared-memory 2D-RoPE rotation of one tile row, plus the R^T un-rotation
-// used by the backward epilogues.
+// 2D-RoPE rotation of shared-memory tiles, R^T un-rotation in the epilogues,
+// and the row-wise helpers the kernels share.
 //
 // A tile is NCH chunks of [128 rows][64 cols] 16-bit elements, each chunk in the
-// 128-byte-swizzled layout TMA writes (granule g of row r at (g ^ (r & 7)) * 16).
-// Pair p of a row is the 32-bit word holding columns (2p, 2p+1); a 16-byte
-// granule holds pairs 4g'..4g'+3, so the swizzle never splits a pair.
+// 128-byte-swizzled layout TMA writes (16-byte granule g of row r at
+// (g ^ (r & 7)) * 16). Pair p of a row is the 32-bit word holding columns
+// (2p, 2p+1); granule g holds pairs 4g .. 4g+3, so the swizzle never splits a
+// pair.
 //
 // Rotation of pair (e, o) with table values (c, s) (fa_rope_full .py:201-202,
-// 271-272):  e' = e c - o s,  o' = o c + e s.  Token t uses table row t - has_cls;
-// the CLS token (t == 0 with has_cls) is left as is (fa_rope_full .py:177-179).
-// The arithmetic is f32 with one rounding to the 16-bit type.
+// 271-272):  e' = e c - o s,  o' = o c + e s.  Token t uses table row
+// t - has_cls; the CLS token (t == 0 with has_cls) is left as is
+// (fa_rope_full .py:177-179). Gradients are un-rotated with R^T
+// (fa_rope_full .py:653-662, 984-993):  e = e^ c + o^ s,  o = o^ c - e^ s.
+// All arithmetic is f32 with one rounding to the 16-bit type.
+//
+// Row-wise work uses a "quad" layout: a warp handles 4 rows per instruction,
+// lane l taking granule (l & 7) of row (l >> 3) of the quad, so every
+// shared-memory access is a conflict-free 16-byte vector and every global
+// access of a row is one coalesced 128-byte line. (With one lane per pair the
+// count of shared-memory instructions, not their latency, bounds these loops.)
 #pragma once
 #include "frsa_ptx.cuh"
 
@@ -22,177 +31,108 @@ __device__ __forceinline__ int rope_pos(int t, int N, int has_cls) {
   return t - has_cls;
 }
 
-// Pull the table rows of token position `pos` toward L1 ahead of use, so the
-// rotation that follows a TMA wait does not pay an L2 round trip per granule.
-__device__ __forceinline__ void prefetch_rope_row(int pos, int D, const float* __restrict__ cosp,
-                                                  const float* __restrict__ sinp) {
-  if (pos < 0) return;
-  const int D2 = D >> 1;
-  const char* c = reinterpret_cast<const char*>(cosp + static_cast<size_t>(pos) * D2);
-  const char* s = reinterpret_cast<const char*>(sinp + static_cast<size_t>(pos) * D2);
-  for (int off = 0; off < D2 * 4; off += 128) {
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(c + off));
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(s + off));
-  }
+// Rotate the four pairs of a granule.
+template <typename T>
+__device__ __forceinline__ uint4 rotate_granule(uint4 x, float4 c, float4 s) {
+  uint4 o;
+  float2 v;
+  v = Elt<T>::unpack(x.x);
+  o.x = Elt<T>::pack(v.x * c.x - v.y * s.x, v.y * c.x + v.x * s.x);
+  v = Elt<T>::unpack(x.y);
+  o.y = Elt<T>::pack(v.x * c.y - v.y * s.y, v.y * c.y + v.x * s.y);
+  v = Elt<T>::unpack(x.z);
+  o.z = Elt<T>::pack(v.x * c.z - v.y * s.z, v.y * c.z + v.x * s.z);
+  v = Elt<T>::unpack(x.w);
+  o.w = Elt<T>::pack(v.x * c.w - v.y * s.w, v.y * c.w + v.x * s.w);
+  return o;
 }
 
-// Rotate row r of a tile in place. Granules are processed four at a time with
-// every shared and table load of the group issued before any store, so the
-// loads overlap (the stores go through a generic pointer the compiler must
-// assume may alias the tables).
-template <typename T, int NCH>
-__device__ __forceinline__ void rotate_row_smem(uint8_t* tile, int r, int D, int pos,
-                                                const float* __restrict__ cosp,
-                                                const float* __restrict__ sinp) {
-  if (pos < 0) return;
-  const int D2 = D >> 1;
-  const float4* crow = reinterpret_cast<const float4*>(cosp + static_cast<size_t>(pos) * D2);
-  const float4* srow = reinterpret_cast<const float4*>(sinp + static_cast<size_t>(pos) * D2);
-  const int ngran = D >> 3;  // 8 elements = 4 pairs per granule
-#pragma unroll
-  for (int g0 = 0; g0 < 8 * NCH; g0 += 4) {
-    if (g0 < ngran) {
-      uint4 w[4];
-      float4 cs[4], sn[4];
-      uint4* ptr[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int gg = g0 + u;
-        ptr[u] = reinterpret_cast<uint4*>(tile + (gg >> 3) * 16384 + sw128_off(r, gg & 7));
-        if (gg < ngran) {
-          w[u] = *ptr[u];
-          cs[u] = __ldg(crow + gg);
-          sn[u] = __ldg(srow + gg);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (g0 + u < ngran) {
-          const float2 a = Elt<T>::unpack(w[u].x), b = Elt<T>::unpack(w[u].y),
-                       cc = Elt<T>::unpack(w[u].z), d = Elt<T>::unpack(w[u].w);
-          const float4 c = cs[u], s = sn[u];
-          uint4 o;
-          o.x = Elt<T>::pack(a.x * c.x - a.y * s.x, a.y * c.x + a.x * s.x);
-          o.y = Elt<T>::pack(b.x * c.y - b.y * s.y, b.y * c.y + b.x * s.y);
-          o.z = Elt<T>::pack(cc.x * c.z - cc.y * s.z, cc.y * c.z + cc.x * s.z);
-          o.w = Elt<T>::pack(d.x * c.w - d.y * s.w, d.y * c.w + d.x * s.w);
-          *ptr[u] = o;
-        }
-      }
-    }
-  }
-}
-
-// R^T on an f32 row held in registers (v[2p], v[2p+1] = gradient of pair p in
-// the rotated basis):  e = e^ c + o^ s,  o = -e^ s + o^ c  (fa_rope_full .py:653-662).
-template <int NV>
-__device__ __forceinline__ void unrotate_row_regs(float (&v)[NV], int D, int pos,
-                                                  const float* __restrict__ cosp,
-                                                  const float* __restrict__ sinp) {
-  if (pos < 0) return;
-  const int D2 = D >> 1;
-  const float* crow = cosp + static_cast<size_t>(pos) * D2;
-  const float* srow = sinp + static_cast<size_t>(pos) * D2;
-#pragma unroll
-  for (int p = 0; p < NV / 2; ++p) {
-    if (p < D2) {
-      const float c = __ldg(crow + p), s = __ldg(srow + p);
-      const float e = v[2 * p], o = v[2 * p + 1];
-      v[2 * p] = e * c + o * s;
-      v[2 * p + 1] = o * c - e * s;
-    }
-  }
-}
-
-// Store an f32 row of D values as 16-bit elements (D % 8 == 0, dst 16-byte aligned).
-template <typename T, int NV>
-__device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], int D) {
-#pragma unroll
-  for (int g = 0; g < NV / 8; ++g) {
-    if (g * 8 < D) {
-      uint4 w;
-      w.x = Elt<T>::pack(v[8 * g + 0], v[8 * g + 1]);
-      w.y = Elt<T>::pack(v[8 * g + 2], v[8 * g + 3]);
-      w.z = Elt<T>::pack(v[8 * g + 4], v[8 * g + 5]);
-      w.w = Elt<T>::pack(v[8 * g + 6], v[8 * g + 7]);
-      reinterpret_cast<uint4*>(dst)[g] = w;
-    }
-  }
-}
-
-}  // namespace frsa
-
-namespace frsa {
-
-// ---------------------------------------------------------------------------
-// Warp-per-row helpers. A warp walks rows [r_begin, r_end) of a tile; lane p
-// owns RoPE pair p (columns 2p, 2p+1), so table reads are coalesced (one
-// 128-byte line per row for D = 64) and shared-memory accesses of a row hit 32
-// distinct banks.
-
-// Byte offset of pair p of row r in a 128B-swizzled chunked tile.
-__device__ __forceinline__ uint32_t sw128_pair_off(uint32_t r, uint32_t p) {
-  const uint32_t c = p >> 5, q = p & 31;
-  return c * 16384u + r * 128u + ((((q >> 2) ^ (r & 7u))) << 4) + ((q & 3u) << 2);
-}
-
-// Table values for the 32 rows a warp rotates, lane p holding pair p
-// (D <= 64) or pairs p and p + 32 (D <= 128). Loaded before the tile's TMA
-// wait so the table latency overlaps the load.
-template <int NCH, int ROWS = 32>
-struct RopeRows {
-  float c[NCH][ROWS], s[NCH][ROWS];
+// Table values for ROWS rows of a tile (ROWS / 4 quads), lane l holding the
+// four pairs of granule (l & 7) (+ 8 h for chunk h) of its row of each quad.
+// Rows that are not rotated hold c = 1, s = 0. Loaded before a tile's TMA wait
+// so the global-memory latency overlaps the load.
+template <int NCH, int ROWS>
+struct RopeQ {
+  float4 c[NCH][ROWS / 4], s[NCH][ROWS / 4];
 };
 
-template <int NCH, int ROWS = 32>
-__device__ __forceinline__ void load_rope_rows(RopeRows<NCH, ROWS>& t, int r_begin, int tok0, int N,
-                                               int has_cls, int D,
-                                               const float* __restrict__ cosp,
-                                               const float* __restrict__ sinp, int lane) {
+template <int NCH, int ROWS>
+__device__ __forceinline__ void load_rope_q(RopeQ<NCH, ROWS>& t, int r_begin, int tok0, int N,
+                                            int has_cls, int D, const float* __restrict__ cosp,
+                                            const float* __restrict__ sinp, int lane) {
   const int D2 = D >> 1;
+  const int rq = lane >> 3, gl = lane & 7;
 #pragma unroll
-  for (int h = 0; h < NCH; ++h) {
-    const int p = lane + 32 * h;
+  for (int k = 0; k < ROWS / 4; ++k) {
+    const int pos = rope_pos(tok0 + r_begin + 4 * k + rq, N, has_cls);
 #pragma unroll
-    for (int u = 0; u < ROWS; ++u) {
-      const int pos = rope_pos(tok0 + r_begin + u, N, has_cls);
-      t.c[h][u] = 1.f;
-      t.s[h][u] = 0.f;
-      if (pos >= 0 && p < D2) {
-        t.c[h][u] = __ldg(cosp + static_cast<size_t>(pos) * D2 + p);
-        t.s[h][u] = __ldg(sinp + static_cast<size_t>(pos) * D2 + p);
+    for (int h = 0; h < NCH; ++h) {
+      const int g = gl + 8 * h;
+      t.c[h][k] = make_float4(1.f, 1.f, 1.f, 1.f);
+      t.s[h][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (pos >= 0 && 8 * g < D) {
+        t.c[h][k] = __ldg(reinterpret_cast<const float4*>(cosp + static_cast<size_t>(pos) * D2) + g);
+        t.s[h][k] = __ldg(reinterpret_cast<const float4*>(sinp + static_cast<size_t>(pos) * D2) + g);
       }
     }
   }
 }
 
-// Rotate the warp's ROWS rows [r_begin, r_begin + ROWS) of a tile in place
-// with preloaded table values (rows that are not rotated carry c = 1, s = 0).
-template <typename T, int NCH, int ROWS = 32>
-__device__ __forceinline__ void apply_rope_rows(uint8_t* tile, int r_begin, int D,
-                                                const RopeRows<NCH, ROWS>& t, int lane) {
-  const int D2 = D >> 1;
+// Rotate rows [r_begin, r_begin + ROWS) of a tile in place with preloaded tables.
+template <typename T, int NCH, int ROWS>
+__device__ __forceinline__ void apply_rope_q(uint8_t* tile, int r_begin, int D,
+                                             const RopeQ<NCH, ROWS>& t, int lane) {
   const uint32_t base = smem_u32(tile);
+  const int rq = lane >> 3, gl = lane & 7;
+  uint4 x[NCH][ROWS / 4];
 #pragma unroll
-  for (int h = 0; h < NCH; ++h) {
-    const int p = lane + 32 * h;
-    if (p < D2) {
-      uint32_t w[ROWS];
+  for (int k = 0; k < ROWS / 4; ++k)
 #pragma unroll
-      for (int u = 0; u < ROWS; ++u) w[u] = lds_u32(base + sw128_pair_off(r_begin + u, p));
+    for (int h = 0; h < NCH; ++h)
+      if (8 * (gl + 8 * h) < D)
+        x[h][k] = lds_u4(base + h * 16384 + sw128_off(r_begin + 4 * k + rq, gl));
 #pragma unroll
-      for (int u = 0; u < ROWS; ++u) {
-        const float2 x = Elt<T>::unpack(w[u]);
-        const float c = t.c[h][u], s = t.s[h][u];
-        sts_u32(base + sw128_pair_off(r_begin + u, p),
-                Elt<T>::pack(x.x * c - x.y * s, x.y * c + x.x * s));
-      }
+  for (int k = 0; k < ROWS / 4; ++k)
+#pragma unroll
+    for (int h = 0; h < NCH; ++h)
+      if (8 * (gl + 8 * h) < D)
+        sts_u4(base + h * 16384 + sw128_off(r_begin + 4 * k + rq, gl),
+               rotate_granule<T>(x[h][k], t.c[h][k], t.s[h][k]));
+}
+
+// Rotate `nrows` rows (a multiple of 16) from r_begin of a one-chunk tile in
+// place, with the tables resident in shared memory as [n_pos][32] f32 (D <= 64).
+template <typename T>
+__device__ __forceinline__ void rotate_q_tabsm(uint32_t tile, int r_begin, int nrows, int tok0,
+                                               int N, int has_cls, int D, uint32_t cos_sm,
+                                               uint32_t sin_sm, int lane) {
+  const int rq = lane >> 3, gl = lane & 7;
+  if (8 * gl >= D) return;
+  for (int u0 = 0; u0 < nrows; u0 += 16) {
+    uint4 x[4];
+    float4 c[4], s[4];
+    int pos[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = r_begin + u0 + 4 * k + rq;
+      pos[k] = rope_pos(tok0 + r, N, has_cls);
+      const int pq = pos[k] < 0 ? 0 : pos[k];
+      c[k] = lds_f4(cos_sm + (pq * 32 + 4 * gl) * 4);
+      s[k] = lds_f4(sin_sm + (pq * 32 + 4 * gl) * 4);
+      x[k] = lds_u4(tile + sw128_off(r, gl));
     }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (pos[k] >= 0)
+        sts_u4(tile + sw128_off(r_begin + u0 + 4 * k + rq, gl),
+               rotate_granule<T>(x[k], c[k], s[k]));
   }
 }
 
-// Row stride and swizzle of the f32 staging tile used by the epilogues:
-// rows of 64*NCH floats, 16-byte chunk c of row r stored at chunk c ^ (r & 7).
+// ---------------------------------------------------------------------------
+// f32 staging tile used by the epilogues: rows of 64*NCH floats, 16-byte chunk
+// c of row r stored at chunk c ^ (r & 7). Rows are written thread-per-row (the
+// TMEM read-out layout) and drained in the quad layout.
 template <int NCH>
 __device__ __forceinline__ uint32_t stage_off(uint32_t r, uint32_t chunk) {
   return r * (256u * NCH) + ((chunk ^ (r & 7u)) << 4);
@@ -208,37 +148,80 @@ __device__ __forceinline__ void stage_write16(uint8_t* stage, int r, int c16, co
            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]));
 }
 
-// Warp-per-row drain of the warp's ROWS staged f32 rows [r_begin, r_begin + ROWS):
-// scale, optional R^T un-rotation with preloaded tables (pass rope = nullptr
-// for none), rounding to T and a coalesced store to dst + tok * D for the rows
-// whose token tok0 + r is < N.
-template <typename T, int NCH, int ROWS = 32>
-__device__ __forceinline__ void drain_rows_warp(const uint8_t* stage, int r_begin, int tok0, int N,
-                                                int D, float scale,
-                                                const RopeRows<NCH, ROWS>* rope, T* dst,
-                                                int lane) {
-  const int D2 = D >> 1;
+// Read granule g (8 floats) of staged row r, scaled.
+template <int NCH>
+__device__ __forceinline__ void stage_read8(uint32_t base, int r, int g, float scale,
+                                            float (&v)[8]) {
+  const float4 a = lds_f4(base + stage_off<NCH>(r, 2 * g));
+  const float4 b = lds_f4(base + stage_off<NCH>(r, 2 * g + 1));
+  v[0] = a.x * scale; v[1] = a.y * scale; v[2] = a.z * scale; v[3] = a.w * scale;
+  v[4] = b.x * scale; v[5] = b.y * scale; v[6] = b.z * scale; v[7] = b.w * scale;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 w;
+  w.x = Elt<T>::pack(v[0], v[1]);
+  w.y = Elt<T>::pack(v[2], v[3]);
+  w.z = Elt<T>::pack(v[4], v[5]);
+  w.w = Elt<T>::pack(v[6], v[7]);
+  return w;
+}
+
+// R^T on the four pairs of a granule held as 8 floats.
+__device__ __forceinline__ void unrotate8(float (&v)[8], float4 c, float4 s) {
+  const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float e = v[2 * p], o = v[2 * p + 1];
+    v[2 * p] = e * cc[p] + o * ss[p];
+    v[2 * p + 1] = o * cc[p] - e * ss[p];
+  }
+}
+
+// Drain staged rows [r_begin, r_begin + ROWS): scale, optional R^T with
+// preloaded tables (rope == nullptr for none), round to T, store to
+// dst + tok * D with tok = tok0 + r (rows with tok >= N are skipped).
+template <typename T, int NCH, int ROWS>
+__device__ __forceinline__ void drain_q(const uint8_t* stage, int r_begin, int tok0, int N, int D,
+                                        float scale, const RopeQ<NCH, ROWS>* rope, T* dst,
+                                        int lane) {
   const uint32_t base = smem_u32(stage);
+  const int rq = lane >> 3, gl = lane & 7;
 #pragma unroll
-  for (int h = 0; h < NCH; ++h) {
-    const int p = lane + 32 * h;
-    if (p < D2) {
+  for (int k = 0; k < ROWS / 4; ++k) {
+    const int r = r_begin + 4 * k + rq;
+    const int tok = tok0 + r;
 #pragma unroll
-      for (int u = 0; u < ROWS; ++u) {
-        const int r = r_begin + u;
-        const int tok = tok0 + r;
-        if (tok < N) {
-          const float2 g = lds_f2(base + stage_off<NCH>(r, p >> 1) + ((p & 1) << 3));
-          float e = g.x * scale, o = g.y * scale;
-          if (rope != nullptr) {
-            const float c = rope->c[h][u], s = rope->s[h][u];
-            const float e2 = e * c + o * s;
-            o = o * c - e * s;
-            e = e2;
-          }
-          reinterpret_cast<uint32_t*>(dst + static_cast<size_t>(tok) * D)[p] = Elt<T>::pack(e, o);
-        }
+    for (int h = 0; h < NCH; ++h) {
+      const int g = gl + 8 * h;
+      if (tok < N && 8 * g < D) {
+        float v[8];
+        stage_read8<NCH>(base, r, g, scale, v);
+        if (rope != nullptr) unrotate8(v, rope->c[h][k], rope->s[h][k]);
+        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(tok) * D + 8 * g) = pack8<T>(v);
       }
+    }
+  }
+}
+
+// Drain one 64-column block of O: the stage (one-chunk layout) holds columns
+// [64 blk, 64 blk + 64) of rows [r_begin, r_begin + ROWS).
+template <typename T, int ROWS>
+__device__ __forceinline__ void drain_block_q(const uint8_t* stage, int r_begin, int tok0, int N,
+                                              int D, int blk, T* dst, int lane) {
+  const uint32_t base = smem_u32(stage);
+  const int rq = lane >> 3, gl = lane & 7;
+  const int g = 8 * blk + gl;
+  if (8 * g >= D) return;
+#pragma unroll
+  for (int k = 0; k < ROWS / 4; ++k) {
+    const int r = r_begin + 4 * k + rq;
+    const int tok = tok0 + r;
+    if (tok < N) {
+      float v[8];
+      stage_read8<1>(base, r, gl, 1.f, v);
+      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(tok) * D + 8 * g) = pack8<T>(v);
     }
   }
 }
