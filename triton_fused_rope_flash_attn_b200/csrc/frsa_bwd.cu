@@ -36,12 +36,18 @@
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
 
+#undef FRSA_STAMP_TID
+#define FRSA_STAMP_TID 128  // first compute thread of this kernel
+
 namespace frsa {
 
 namespace {
 
-constexpr int kComputeThreads = 256;                 // two warpgroups
-constexpr int kBwdThreads = 64 + kComputeThreads;    // + producer warp + MMA warp
+constexpr int kComputeThreads = 256;                  // two warpgroups (warps 4..11)
+constexpr int kBwdThreads = 128 + kComputeThreads;    // + warpgroup 0: producer, MMA, 2 idle
+// Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0 then
+// drops to 96 and the two compute warpgroups rise to 200: 128*96 + 256*200 = 63488.
+constexpr uint32_t kRegsCtl = 96, kRegsCompute = 200;
 constexpr int kRowsPerWarp = kTile / (kComputeThreads / 32);  // 16
 constexpr uint32_t kTmemColsBwd = 512;
 
@@ -59,7 +65,7 @@ struct BwdSmem {
   float delta[QS][kTile];
   uint64_t kv_full[KVS], kv_empty[KVS];
   uint64_t q_full[QS], q_empty[QS];
-  uint64_t kq_ready, st_full, ds_full, mm_done, tm_free, acc_free;
+  uint64_t kq_ready, st_full, ds_full, mm_done, tm_free, acc_free, dq_free;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -74,7 +80,7 @@ struct BwdParams {
   void* dk;
   void* dv;
   float* dq_accum;
-  int N, D, nqt, nkv, has_cls;
+  int BH, N, D, nqt, nkv, has_cls;
   float c2;     // scale * log2(e)
   float scale;
 };
@@ -83,7 +89,7 @@ template <typename T, int NCH, bool RESIDENT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-               const BwdParams prm) {
+               const __grid_constant__ CUtensorMap tm_o, const BwdParams prm) {
   using Sm = BwdSmem<NCH>;
   constexpr int KVS = Sm::KVS;
   constexpr int QS = Sm::QS;
@@ -99,16 +105,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int DP = (D + 15) & ~15;
   const int ksteps = DP >> 4;
   const int nqt = prm.nqt;
-  int bh, j0, nj;
-  if (RESIDENT) {
-    bh = blockIdx.x;
-    j0 = 0;
-    nj = prm.nkv;
-  } else {
-    bh = blockIdx.x / prm.nkv;
-    j0 = blockIdx.x - bh * prm.nkv;
-    nj = 1;
-  }
+  // Work units: resident mode = one head (all key tiles), walked persistently
+  // (unit = blockIdx.x, blockIdx.x + gridDim.x, ...); atomic mode = one
+  // (head, key tile) per CTA.
+  const int nunits = RESIDENT ? prm.BH : prm.BH * prm.nkv;
+  const int nj = RESIDENT ? prm.nkv : 1;
+  auto unit_head = [&](int u) { return RESIDENT ? u : u / prm.nkv; };
+  auto unit_j0 = [&](int u) { return RESIDENT ? 0 : u - (u / prm.nkv) * prm.nkv; };
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
@@ -127,6 +130,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&sm.mm_done, 1);
     mbar_init(&sm.tm_free, 1);
     mbar_init(&sm.acc_free, 1);
+    mbar_init(&sm.dq_free, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -140,6 +144,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + DP;
 
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -147,25 +153,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      int qi = 0;
-      for (int jj = 0; jj < nj; ++jj) {
-        const int j = j0 + jj, ks = jj % KVS;
-        mbar_wait(&sm.kv_empty[ks], ((jj / KVS) & 1) ^ 1, abort_flag);
-        mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
-          tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
-        }
-        for (int i = 0; i < nqt; ++i) {
-          if (RESIDENT && jj > 0) continue;
-          const int qs = RESIDENT ? i : qi % QS;
-          mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
-          mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
-          for (int c = 0; c < NCH; ++c) {
-            tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
-            tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+      tma_prefetch_desc(&tm_o);
+      int qi = 0, kvi = 0;
+      for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+        const int bh = unit_head(u), j0 = unit_j0(u);
+        if (RESIDENT) {
+          // O rows feed Delta in the compute warps: pull this head's and the
+          // next head's O into L2 ahead of those loads.
+          for (int i = 0; i < nqt; ++i) {
+            for (int c = 0; c < NCH; ++c) {
+              if (u == (int)blockIdx.x) tma_prefetch_l2_3d(&tm_o, c * kChunkCols, i * kTile, bh);
+              if (u + (int)gridDim.x < nunits)
+                tma_prefetch_l2_3d(&tm_o, c * kChunkCols, i * kTile, unit_head(u + gridDim.x));
+            }
           }
-          ++qi;
+        }
+        for (int jj = 0; jj < nj; ++jj, ++kvi) {
+          const int j = j0 + jj, ks = kvi % KVS;
+          mbar_wait(&sm.kv_empty[ks], ((kvi / KVS) & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
+          for (int c = 0; c < NCH; ++c) {
+            tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+            tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+          }
+          for (int i = 0; i < nqt; ++i) {
+            if (RESIDENT && jj > 0) continue;
+            const int qs = qi % QS;
+            mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
+            mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
+            for (int c = 0; c < NCH; ++c) {
+              tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+              tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+            }
+            ++qi;
+          }
         }
       }
     }
@@ -176,88 +197,118 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);   // S^T, dP^T
       const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
       const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
-      int it = 0, qi = 0;
-      for (int jj = 0; jj < nj; ++jj) {
-        const int ks = jj % KVS;
-        for (int i = 0; i < nqt; ++i) {
-          const bool fresh = !(RESIDENT && jj > 0);
-          const int qs = RESIDENT ? i : qi % QS;
-          mbar_wait(&sm.kq_ready, it & 1, abort_flag);
-          tc_fence_after();
-          if (it > 0) {
-            mbar_wait(&sm.tm_free, (it - 1) & 1, abort_flag);
+      int it = 0, qi = 0, kvi = 0, hl = 0;
+      for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++hl) {
+        const int qbase = qi;
+        for (int jj = 0; jj < nj; ++jj, ++kvi) {
+          const int ks = kvi % KVS;
+          for (int i = 0; i < nqt; ++i) {
+            const bool fresh = !(RESIDENT && jj > 0);
+            const int qs = RESIDENT ? (qbase + i) % QS : qi % QS;
+            mbar_wait(&sm.kq_ready, it & 1, abort_flag);
             tc_fence_after();
-          }
-          for (int kk = 0; kk < ksteps; ++kk) {
-            const int c = kk >> 2;
-            const uint32_t koff = (kk & 3) * 32;
-            mma_ss(tST, sw128_desc(smem_u32(sm.k[ks][c]) + koff, 16, 1024),
-                   sw128_desc(smem_u32(sm.q[qs][c]) + koff, 16, 1024), idS, kk > 0);
-          }
-          for (int kk = 0; kk < ksteps; ++kk) {
-            const int c = kk >> 2;
-            const uint32_t koff = (kk & 3) * 32;
-            mma_ss(tDPT, sw128_desc(smem_u32(sm.v[ks][c]) + koff, 16, 1024),
-                   sw128_desc(smem_u32(sm.dO[qs][c]) + koff, 16, 1024), idS, kk > 0);
-          }
-          mma_commit(&sm.st_full);
-          mbar_wait(&sm.ds_full, it & 1, abort_flag);
-          tc_fence_after();
-          if (i == 0 && jj > 0) {
-            mbar_wait(&sm.acc_free, (jj - 1) & 1, abort_flag);
+            if (it > 0) {
+              mbar_wait(&sm.tm_free, (it - 1) & 1, abort_flag);
+              tc_fence_after();
+            }
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const int c = kk >> 2;
+              const uint32_t koff = (kk & 3) * 32;
+              mma_ss(tST, sw128_desc(smem_u32(sm.k[ks][c]) + koff, 16, 1024),
+                     sw128_desc(smem_u32(sm.q[qs][c]) + koff, 16, 1024), idS, kk > 0);
+            }
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const int c = kk >> 2;
+              const uint32_t koff = (kk & 3) * 32;
+              mma_ss(tDPT, sw128_desc(smem_u32(sm.v[ks][c]) + koff, 16, 1024),
+                     sw128_desc(smem_u32(sm.dO[qs][c]) + koff, 16, 1024), idS, kk > 0);
+            }
+            mma_commit(&sm.st_full);
+            mbar_wait(&sm.ds_full, it & 1, abort_flag);
             tc_fence_after();
+            if (i == 0 && kvi > 0) {
+              // dV/dK of the previous key tile have been read out.
+              mbar_wait(&sm.acc_free, (kvi - 1) & 1, abort_flag);
+              tc_fence_after();
+            }
+            if (RESIDENT && jj == 0 && i == 0 && hl > 0) {
+              // dQ of the previous head has been read out.
+              mbar_wait(&sm.dq_free, (hl - 1) & 1, abort_flag);
+              tc_fence_after();
+            }
+            for (int kk = 0; kk < kTile / 16; ++kk) {
+              const uint32_t aoff = (kk & 3) * 32;
+              const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
+              // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
+              mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
+                     sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV,
+                     acc);
+              // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
+              mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
+                     sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV,
+                     acc);
+            }
+            // dQ^ (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
+            const uint32_t tDQ = RESIDENT ? (tmem + 384 + 64 * i) : tDPT;
+            for (int kk = 0; kk < kTile / 16; ++kk) {
+              const uint32_t acc =
+                  RESIDENT ? ((jj == 0 && kk == 0) ? 0u : 1u) : (kk > 0 ? 1u : 0u);
+              mma_ss(tDQ, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
+                     sw128_desc(smem_u32(sm.k[ks][0]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
+            }
+            mma_commit(&sm.mm_done);
+            if (!RESIDENT || jj == nj - 1) mma_commit(&sm.q_empty[qs]);
+            if (i == nqt - 1) mma_commit(&sm.kv_empty[ks]);
+            ++it;
+            if (fresh) ++qi;
           }
-          for (int kk = 0; kk < kTile / 16; ++kk) {
-            const uint32_t aoff = (kk & 3) * 32;
-            const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-            // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
-            mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
-                   sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
-            // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
-            mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
-                   sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
-          }
-          // dQ^ (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
-          const uint32_t tDQ = RESIDENT ? (tmem + 384 + 64 * i) : tDPT;
-          for (int kk = 0; kk < kTile / 16; ++kk) {
-            const uint32_t acc = RESIDENT ? ((jj == 0 && kk == 0) ? 0u : 1u) : (kk > 0 ? 1u : 0u);
-            mma_ss(tDQ, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
-                   sw128_desc(smem_u32(sm.k[ks][0]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
-          }
-          mma_commit(&sm.mm_done);
-          if (!RESIDENT) mma_commit(&sm.q_empty[qs]);
-          if (i == nqt - 1) mma_commit(&sm.kv_empty[ks]);
-          ++it;
-          if (fresh) ++qi;
         }
       }
     }
+  }
   } else {
+    setmaxnreg_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute warps
-    // Two warpgroups (warps 2..9). For TMEM reads a thread owns row r (its
+    // Two warpgroups (warps 4..11). For TMEM reads a thread owns row r (its
     // lane quarter wq); warpgroup g takes S/dP columns [64g, 64g + 64) and
     // every other 16-column block of the epilogue tiles. Warp-per-row phases
     // (rotation, Delta, drains) give each of the 8 warps 16 rows.
     constexpr int RW = kRowsPerWarp;
-    const int cw = warp - 2;                       // compute warp 0..7
+    const int cw = warp - 4;                       // compute warp 0..7
     const int g = cw >> 2;                         // warpgroup 0..1
     const int wq = warp & 3;                       // TMEM lane quarter
     const int r = wq * 32 + lane;
     const int rw0 = cw * RW;                       // first row of this warp's row slice
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const bool leader = threadIdx.x == 64;
+    const bool leader = threadIdx.x == 128;
     const float c2 = prm.c2;
-    const int D2 = D >> 1;
-    const size_t head_row0 = static_cast<size_t>(bh) * N;
+    int bh = 0, j0 = 0;          // current unit (set at the top of the unit loop)
+    int it = 0, qi = 0, kvi = 0, hl = 0;  // running iteration / load / unit counters
+    size_t head_row0 = 0;
 
-    // Rotate key tile jj_ of this CTA in its stage.
-    auto prep_k = [&](int jj_) {
-      RopeQ<NCH, RW> rope;
-      const int kv0_ = (j0 + jj_) * kTile;
-      load_rope_q<NCH, RW>(rope, rw0, kv0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.kv_full[jj_ % KVS], (jj_ / KVS) & 1, abort_flag);
-      FRSA_STAMP(22 + (jj_ & 1));
-      apply_rope_q<T, NCH, RW>(&sm.k[jj_ % KVS][0][0], rw0, D, rope, lane);
+    // Resident mode: this warp always handles the same 16-row slices of token
+    // tiles 0 and 1, so its table values are the same for every head; they
+    // are loaded once and kept in registers for the kernel's lifetime.
+    RopeQ<NCH, RW> tab[RESIDENT ? 2 : 1];
+    if (RESIDENT) {
+#pragma unroll
+      for (int t = 0; t < (RESIDENT ? 2 : 1); ++t)
+        load_rope_q<NCH, RW>(tab[t], rw0, t * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
+                             lane);
+    }
+
+    // Rotate key tile j_ (the kvi_-th key/value load) in its stage.
+    auto prep_k = [&](int j_, int kvi_) {
+      if (RESIDENT) {
+        mbar_wait(&sm.kv_full[kvi_ % KVS], (kvi_ / KVS) & 1, abort_flag);
+        if (j_ & 1) apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, tab[RESIDENT ? 1 : 0], lane);
+        else apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, tab[0], lane);
+      } else {
+        RopeQ<NCH, RW> rope;
+        load_rope_q<NCH, RW>(rope, rw0, j_ * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        mbar_wait(&sm.kv_full[kvi_ % KVS], (kvi_ / KVS) & 1, abort_flag);
+        apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, rope, lane);
+      }
     };
     // Prepare query tile i_ in stage qs_ (the qi_-th query load): lse2 (+inf
     // for padded rows, so their P is exactly 0), rotation of Q, and Delta.
@@ -281,10 +332,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                                                 (head_row0 + tok) * D) + gg)
                          : make_uint4(0u, 0u, 0u, 0u);
         }
-      RopeQ<NCH, RW> rope;
-      load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
-      apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      if (RESIDENT) {
+        if (hl == 1 && i_ == 0) FRSA_STAMP(18);
+        mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
+        if (hl == 1 && i_ == 0) FRSA_STAMP(19);
+        if (i_ & 1) apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, tab[RESIDENT ? 1 : 0], lane);
+        else apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, tab[0], lane);
+      } else {
+        RopeQ<NCH, RW> rope;
+        load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
+        apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      }
+      if (hl == 1 && i_ == 0) FRSA_STAMP(20);
       // Delta = sum_d O dO per query row: each lane dots its granule of O with
       // the same granule of the (unrotated) dO tile; 8 lanes share a row.
       const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
@@ -314,15 +374,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             prm.delta_out[head_row0 + q0_ + rr] = dl;
         }
       }
+      if (hl == 1 && i_ == 0) FRSA_STAMP(21);
     };
 
-    // First iteration's operands, then one iteration of look-ahead: the next
-    // key/query tile is prepared while the tensor core computes S^T and dP^T.
-    int it = 0, qi = 0;
-    prep_k(0);
-    prep_q(0, 0, 0);
-    qi = 1;
-    int cur_qs = 0;
+    // Per unit: the first iteration's operands, then one iteration of
+    // look-ahead: the next key/query tile is prepared while the tensor core
+    // computes S^T and dP^T.
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++hl) {
+    bh = unit_head(u);
+    j0 = unit_j0(u);
+    head_row0 = static_cast<size_t>(bh) * N;
+    const int qbase = qi, kvbase = kvi, itbase = it;
+    if (hl == 1) FRSA_STAMP(16);
+    prep_k(j0, kvbase);
+    if (hl == 1) FRSA_STAMP(17);
+    prep_q(0, qi % QS, qi);
+    ++qi;
+    int cur_qs = qbase % QS;
     fence_proxy_async_smem();
     named_bar(1, kComputeThreads);
     if (leader) mbar_arrive(&sm.kq_ready);
@@ -339,9 +407,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         auto prep_next = [&]() {
           const int nj_ = (i + 1 < nqt) ? jj : jj + 1;
           const int ni = (i + 1 < nqt) ? i + 1 : 0;
-          if (ni == 0) prep_k(nj_);
+          if (ni == 0) prep_k(j0 + nj_, kvbase + nj_);
           const bool nfresh = !(RESIDENT && nj_ > 0);
-          const int nqs = RESIDENT ? ni : qi % QS;
+          const int nqs = RESIDENT ? (qbase + ni) % QS : qi % QS;
           if (nfresh) {
             prep_q(ni, nqs, qi);
             ++qi;
@@ -350,10 +418,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         };
         const bool prep_late = has_next && (QS == 1 || KVS == 1);
         if (has_next && !prep_late) prep_next();
-        if (it < 5) FRSA_STAMP(1 + it * 4 + 0);
+        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 0);
 
         mbar_wait(&sm.st_full, it & 1, abort_flag);
-        if (it < 5) FRSA_STAMP(1 + it * 4 + 1);
+        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 1);
         tc_fence_after();
         if (it > 0) mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);  // P/dS tiles free
         {
@@ -412,7 +480,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (has_next && !prep_late) mbar_arrive(&sm.kq_ready);
           }
         }
-        if (it < 5) FRSA_STAMP(1 + it * 4 + 2);
+        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 2);
         if (!RESIDENT) {
           // dQ^ partial of this (key tile, query tile): scale and add into the workspace.
           mbar_wait(&sm.mm_done, it & 1, abort_flag);
@@ -464,9 +532,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       // dV, dK epilogue of key tile j
       RopeQ<NCH, RW> rope_k;
-      load_rope_q<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      if (!RESIDENT) load_rope_q<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
       mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
-      FRSA_STAMP(24 + jj);
       tc_fence_after();
       {
         // TMEM rows -> f32 staging (P/dS tiles, free now) -> warp-per-row drain.
@@ -500,21 +567,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         named_bar(1, kComputeThreads);
         if (NCH == 1)
           drain_q<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, static_cast<const RopeQ<NCH, RW>*>(nullptr), dv_head, lane);
-        drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
+        if (RESIDENT && (j & 1))
+          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &tab[RESIDENT ? 1 : 0], dk_head, lane);
+        else if (RESIDENT)
+          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &tab[0], dk_head, lane);
+        else
+          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
       }
       tc_fence_before();
       named_bar(1, kComputeThreads);
       if (leader) mbar_arrive(&sm.acc_free);
-      FRSA_STAMP(26 + jj);
+      if (hl == 0) FRSA_STAMP(hl * 15 + 12 + jj);
+      ++kvi;
     }
     if (RESIDENT) {
       // dQ epilogue: every MMA has completed (last mm_done waited above).
       uint8_t* stage = &sm.p[0][0];
       T* dq_head = reinterpret_cast<T*>(prm.dq) + head_row0 * D;
       for (int i = 0; i < nqt; ++i) {
-        RopeQ<NCH, RW> rope_q;
-        load_rope_q<NCH, RW>(rope_q, rw0, i * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
-                                lane);
+
 #pragma unroll 1
         for (int c16 = g; c16 < 4; c16 += 2) {
           if (c16 * 16 < DP) {
@@ -525,14 +596,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
         named_bar(1, kComputeThreads);
-        drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &rope_q, dq_head,
-                                    lane);
+        if (i & 1)
+          drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &tab[RESIDENT ? 1 : 0],
+                              dq_head, lane);
+        else
+          drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &tab[0], dq_head, lane);
+        tc_fence_before();
         named_bar(1, kComputeThreads);
       }
+      if (leader) mbar_arrive(&sm.dq_free);
+      if (hl == 0) FRSA_STAMP(hl * 15 + 14);
     }
+    }  // unit loop
   }
 
   FRSA_STAMP(30);
+  tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -585,21 +664,29 @@ namespace {
 template <typename T, int NCH, bool RESIDENT>
 cudaError_t launch_bwd_main(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                             const CUtensorMap& tm_v, const CUtensorMap& tm_do,
-                            const BwdParams& p, cudaStream_t stream) {
+                            const CUtensorMap& tm_o, const BwdParams& p, cudaStream_t stream) {
   const size_t smem = sizeof(BwdSmem<NCH>) + 1024;
   auto kern = bwd_kernel<T, NCH, RESIDENT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const long long grid = RESIDENT ? static_cast<long long>(s.BH)
+  int nsm = 148;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const long long grid = RESIDENT ? static_cast<long long>(s.BH < nsm ? s.BH : nsm)
                                   : static_cast<long long>(s.BH) * p.nkv;
-  kern<<<static_cast<unsigned>(grid), kBwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, p);
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, tm_o,
+                                                                     p);
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                         const CUtensorMap& tm_v, const CUtensorMap& tm_do, const void* o,
+                         const CUtensorMap& tm_v, const CUtensorMap& tm_do,
+                         const CUtensorMap& tm_o, const void* o,
                          const void* d_o, const float* lse, float* delta, const float* cosp,
                          const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
                          cudaStream_t stream) {
@@ -615,6 +702,7 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.dk = dk;
   p.dv = dv;
   p.dq_accum = dq_accum;
+  p.BH = s.BH;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
@@ -624,12 +712,13 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.scale = s.scale;
   cudaError_t e;
   if (!bwd_needs_workspace(s)) {
-    return launch_bwd_main<T, 1, true>(s, tm_q, tm_k, tm_v, tm_do, p, stream);
+    return launch_bwd_small(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, lse, delta, cosp, sinp, dq, dk,
+                            dv, stream);
   }
   e = cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
   if (e != cudaSuccess) return e;
-  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream)
-                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream);
+  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream)
+                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream);
   if (e != cudaSuccess) return e;
   const int threads = 256;
   const long long total = rows * (s.D >> 3);
@@ -642,14 +731,15 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
 }  // namespace
 
 cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const void* o,
+                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                       const void* o,
                        const void* d_o, const float* lse, float* delta, const float* cosp,
                        const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
                        cudaStream_t stream) {
   if (s.bf16)
-    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, o, d_o, lse, delta, cosp, sinp,
+    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, d_o, lse, delta, cosp, sinp,
                                        dq, dk, dv, dq_accum, stream);
-  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, o, d_o, lse, delta, cosp, sinp, dq, dk,
+  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, d_o, lse, delta, cosp, sinp, dq, dk,
                               dv, dq_accum, stream);
 }
 

@@ -156,6 +156,9 @@ __global__ void __launch_bounds__(kFsThreads, 1)
         mbar_wait(&sm.k_ready[0], hp, abort_flag);
         tc_fence_after();
         for (int g = 0; g < nqt; ++g) issue_s(g, 0);
+        // The Q tiles are free for the next head once the last S MMA reading
+        // them completes, long before this head's P V products.
+        if (nkv == 1) mma_commit(&sm.q_empty);
         for (int j = 0; j < nkv; ++j) {
           const int c = hl * nkv + j;
           for (int g = 0; g < nqt; ++g) {
@@ -168,11 +171,11 @@ __global__ void __launch_bounds__(kFsThreads, 1)
                 tc_fence_after();
               }
               issue_s(g, j + 1);
+              if (j + 2 == nkv && g == nqt - 1) mma_commit(&sm.q_empty);
             }
           }
           mma_commit(&sm.kv_empty[j]);
         }
-        mma_commit(&sm.q_empty);
       }
     }
   } else if (warp < 4) {

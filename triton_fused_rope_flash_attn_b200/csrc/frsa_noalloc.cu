@@ -64,7 +64,8 @@ float* noalloc_scratch_ptr() {
 template <typename T>
 cudaError_t launch_bwd_accum_t(const LaunchShape& s, const CUtensorMap& tm_q,
                                const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                               const CUtensorMap& tm_do, const void* o, const float* lse,
+                               const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                               const void* o, const float* lse,
                                float* delta, const float* cosp, const float* sinp, void* dq,
                                void* dk, void* dv, float* dq_accum, cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
@@ -78,6 +79,7 @@ cudaError_t launch_bwd_accum_t(const LaunchShape& s, const CUtensorMap& tm_q,
   p.dk = dk;
   p.dv = dv;
   p.dq_accum = dq_accum;
+  p.BH = s.BH;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
@@ -88,8 +90,8 @@ cudaError_t launch_bwd_accum_t(const LaunchShape& s, const CUtensorMap& tm_q,
   cudaError_t e =
       cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
   if (e != cudaSuccess) return e;
-  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream)
-                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, p, stream);
+  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream)
+                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream);
   if (e != cudaSuccess) return e;
   const int threads = 256;
   const long long total = rows * (s.D >> 3);
@@ -118,16 +120,16 @@ extern "C" int frsa_bwd_noalloc(const frsa_attn_args* a, void* stream) {
   float* scratch = frsa::noalloc_scratch_ptr();
   if (scratch == nullptr) return launch_error("frsa_bwd_noalloc: cudaGetSymbolAddress", cudaGetLastError());
   (void)cudaGetLastError();
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, to;
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
-      !encode_map(&tdo, a->d_o, s))
+      !encode_map(&tdo, a->d_o, s) || !encode_map(&to, a->o, s))
     return launch_error("frsa_bwd_noalloc", cudaSuccess);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t e =
-      s.bf16 ? frsa::launch_bwd_accum_t<__nv_bfloat16>(s, tq, tk, tv, tdo, a->o, a->lse, a->delta,
+      s.bf16 ? frsa::launch_bwd_accum_t<__nv_bfloat16>(s, tq, tk, tv, tdo, to, a->o, a->lse, a->delta,
                                                        a->cosp, a->sinp, a->dq, a->dk, a->dv,
                                                        scratch, st)
-             : frsa::launch_bwd_accum_t<__half>(s, tq, tk, tv, tdo, a->o, a->lse, a->delta,
+             : frsa::launch_bwd_accum_t<__half>(s, tq, tk, tv, tdo, to, a->o, a->lse, a->delta,
                                                 a->cosp, a->sinp, a->dq, a->dk, a->dv, scratch,
                                                 st);
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd_noalloc", e);

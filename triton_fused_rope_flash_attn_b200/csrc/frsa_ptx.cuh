@@ -170,6 +170,24 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// Hint the tile {x, y, z} of a 3-D tensor map into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// Per-warpgroup register rebalancing (all 128 threads of a warpgroup execute it).
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
+}
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
+}
+
 // ---------------------------------------------------------------- tcgen05
 // TMEM allocation: writes the base address to *slot (shared). Whole warp.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

@@ -227,3 +227,87 @@ __device__ __forceinline__ void drain_block_q(const uint8_t* stage, int r_begin,
 }
 
 }  // namespace frsa
+
+namespace frsa {
+
+// ---------------------------------------------------------------------------
+// Thread-per-row helpers (thread = tile row = TMEM lane), used where a row's
+// values arrive in one thread's registers from TMEM. Table values live in a
+// shared "table tile" laid out like a data tile: granule g of row r holds the
+// four pairs 4g..4g+3 of that row as packed f16 (cos, sin) (low half cos).
+// cos and sin lie in [-1, 1], so f16 keeps them to ~2^-11 relative, far below
+// the 16-bit rounding of the rotated values themselves.
+
+// Write row r of a table tile for token position pos (pos < 0: identity).
+__device__ __forceinline__ void store_tabrow(uint32_t tab, int r, int pos, int D,
+                                             const float* __restrict__ cosp,
+                                             const float* __restrict__ sinp) {
+  const int D2 = D >> 1;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    float4 c = make_float4(1.f, 1.f, 1.f, 1.f), s = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (pos >= 0 && 8 * g < D) {
+      c = __ldg(reinterpret_cast<const float4*>(cosp + static_cast<size_t>(pos) * D2) + g);
+      s = __ldg(reinterpret_cast<const float4*>(sinp + static_cast<size_t>(pos) * D2) + g);
+    }
+    sts_u4(tab + sw128_off(r, g),
+           make_uint4(Elt<__half>::pack(c.x, s.x), Elt<__half>::pack(c.y, s.y),
+                      Elt<__half>::pack(c.z, s.z), Elt<__half>::pack(c.w, s.w)));
+  }
+}
+
+// Rotate row r of a one-chunk tile in place with table tile `tab`.
+template <typename T>
+__device__ __forceinline__ void rotate_row_t(uint32_t tile, uint32_t tab, int r, int D) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    if (8 * g < D) {
+      const uint4 x = lds_u4(tile + sw128_off(r, g));
+      const uint4 t = lds_u4(tab + sw128_off(r, g));
+      const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, tw[4] = {t.x, t.y, t.z, t.w};
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 cs = Elt<__half>::unpack(tw[e]);
+        const float2 v = Elt<T>::unpack(xw[e]);
+        w[e] = Elt<T>::pack(v.x * cs.x - v.y * cs.y, v.y * cs.x + v.x * cs.y);
+      }
+      sts_u4(tile + sw128_off(r, g), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  }
+}
+
+// Scale (and with tab != 0 R^T-unrotate) a row of 64 f32 values, given as two
+// 32-value halves, and store it.
+template <typename T>
+__device__ __forceinline__ void store_row_t(const float (&v0)[32], const float (&v1)[32], int D,
+                                            float scale, uint32_t tab, int r, T* dst) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    if (8 * g < D) {
+      uint32_t tw[4] = {0u, 0u, 0u, 0u};
+      if (tab != 0u) {
+        const uint4 t = lds_u4(tab + sw128_off(r, g));
+        tw[0] = t.x; tw[1] = t.y; tw[2] = t.z; tw[3] = t.w;
+      }
+      float u[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 8 * g + 2 * e;
+        float a = (c < 32 ? v0[c & 31] : v1[c & 31]) * scale;
+        float b = (c < 32 ? v0[(c + 1) & 31] : v1[(c + 1) & 31]) * scale;
+        if (tab != 0u) {
+          const float2 cs = Elt<__half>::unpack(tw[e]);
+          const float a2 = a * cs.x + b * cs.y;
+          b = b * cs.x - a * cs.y;
+          a = a2;
+        }
+        u[2 * e] = a;
+        u[2 * e + 1] = b;
+      }
+      reinterpret_cast<uint4*>(dst)[g] = pack8<T>(u);
+    }
+  }
+}
+
+}  // namespace frsa
