@@ -157,10 +157,11 @@ int frsa_fwd(const frsa_attn_args* a, void* stream) {
   // A non-sticky error left on this host thread by an earlier runtime call
   // (e.g. cudaErrorNotReady from an event poll) must not be blamed on our launch.
   (void)cudaGetLastError();
-  CUtensorMap tq, tk, tv;
-  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s))
+  CUtensorMap tq, tk, tv, to;
+  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
+      !encode_map(&to, a->o, s))
     return launch_error("frsa_fwd", cudaSuccess);
-  const cudaError_t e = frsa::launch_fwd(s, tq, tk, tv, a->cosp, a->sinp, a->o, a->lse,
+  const cudaError_t e = frsa::launch_fwd(s, tq, tk, tv, to, a->cosp, a->sinp, a->o, a->lse,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_fwd", e);
 }

@@ -22,15 +22,17 @@ struct LaunchShape {
 };
 
 // Forward. tm_q/k/v: 3-D maps {D, N, BH} with box {64, 128, 1}, 128B swizzle.
+// tm_o: the same map over O (used by the persistent kernel's TMA store).
 cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                       const CUtensorMap& tm_v, const float* cosp, const float* sinp, void* o,
-                       float* lse, cudaStream_t stream);
+                       const CUtensorMap& tm_v, const CUtensorMap& tm_o, const float* cosp,
+                       const float* sinp, void* o, float* lse, cudaStream_t stream);
 
 // Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
 bool fwd_small_applies(const LaunchShape& s);
 cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
-                             const CUtensorMap& tm_k, const CUtensorMap& tm_v, const float* cosp,
-                             const float* sinp, void* o, float* lse, cudaStream_t stream);
+                             const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                             const CUtensorMap& tm_o, const float* cosp, const float* sinp,
+                             float* lse, cudaStream_t stream);
 
 // Persistent backward for N <= 256, D <= 64 (dQ reduced on chip).
 cudaError_t launch_bwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
