@@ -184,11 +184,14 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
   }
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
   (void)cudaGetLastError();  // see frsa_fwd
-  CUtensorMap tq, tk, tv, tdo, to;
+  CUtensorMap tq, tk, tv, tdo, to, tgrads[3];
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
       !encode_map(&tdo, a->d_o, s) || !encode_map(&to, a->o, s))
     return launch_error("frsa_bwd", cudaSuccess);
-  const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, to, a->o, a->d_o, a->lse, a->delta,
+  if (ws == nullptr && (!encode_map(&tgrads[0], a->dq, s) || !encode_map(&tgrads[1], a->dk, s) ||
+                        !encode_map(&tgrads[2], a->dv, s)))
+    return launch_error("frsa_bwd", cudaSuccess);
+  const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, to, a->o, ws ? nullptr : tgrads, a->d_o, a->lse, a->delta,
                                          a->cosp, a->sinp, a->dq, a->dk, a->dv, ws,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);

@@ -687,9 +687,9 @@ template <typename T>
 cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                          const CUtensorMap& tm_v, const CUtensorMap& tm_do,
                          const CUtensorMap& tm_o, const void* o,
-                         const void* d_o, const float* lse, float* delta, const float* cosp,
-                         const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
-                         cudaStream_t stream) {
+                         const CUtensorMap* tm_grads, const void* d_o, const float* lse,
+                         float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
+                         void* dv, float* dq_accum, cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
   (void)d_o;
   BwdParams p;
@@ -712,8 +712,9 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.scale = s.scale;
   cudaError_t e;
   if (!bwd_needs_workspace(s)) {
-    return launch_bwd_small(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, lse, delta, cosp, sinp, dq, dk,
-                            dv, stream);
+    if (tm_grads == nullptr) return cudaErrorInvalidValue;
+    return launch_bwd_small(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads, o, lse, delta, cosp, sinp,
+                            dq, dk, dv, stream);
   }
   e = cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
   if (e != cudaSuccess) return e;
@@ -732,15 +733,15 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
 
 cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                        const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
-                       const void* o,
+                       const void* o, const CUtensorMap* tm_grads,
                        const void* d_o, const float* lse, float* delta, const float* cosp,
                        const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
                        cudaStream_t stream) {
   if (s.bf16)
-    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, d_o, lse, delta, cosp, sinp,
-                                       dq, dk, dv, dq_accum, stream);
-  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, d_o, lse, delta, cosp, sinp, dq, dk,
-                              dv, dq_accum, stream);
+    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse,
+                                       delta, cosp, sinp, dq, dk, dv, dq_accum, stream);
+  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse, delta, cosp,
+                              sinp, dq, dk, dv, dq_accum, stream);
 }
 
 }  // namespace frsa

@@ -60,7 +60,7 @@ struct BsSmem {
   uint64_t kv_full[2], kv_empty[2], k_ready[2];
   uint64_t q_full[2], q_empty[2], q_ready[2];
   uint64_t st_full, tm_free, ds_full, pds_free;
-  uint64_t acc_full[2], acc_free, dq_full, dq_free;
+  uint64_t acc_full[2], acc_free, dq_full[2], dq_free[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -85,6 +85,7 @@ template <typename T>
 __device__ __forceinline__ void bs_prep_k(BsSmem& sm, int j, int hl, int r, int D, bool leader,
                                           volatile int* abort_flag) {
   mbar_wait(&sm.kv_full[j], hl & 1, abort_flag);
+  if (hl == 1 && j == 0) FRSA_STAMP(25);
   rotate_row_t<T>(smem_u32(sm.k[j]), smem_u32(sm.tab[j]), r, D);
   fence_proxy_async_smem();
   named_bar(2, 128);
@@ -107,9 +108,11 @@ __device__ __forceinline__ void bs_prep_q(BsSmem& sm, const BsParams& prm, int i
   for (int g = 0; g < 8; ++g)
     og[g] = (qv && 8 * g < D) ? __ldg(orow + g) : make_uint4(0u, 0u, 0u, 0u);
   mbar_wait(&sm.q_full[i], hl & 1, abort_flag);
+  if (hl == 1 && i == 0) FRSA_STAMP(26);
   // Padded query rows get lse2 = +inf, so their P (and dS) is exactly 0.
   sm.lse2[i][r] = qv ? lsev * 1.4426950408889634f : INFINITY;
   rotate_row_t<T>(smem_u32(sm.q[i]), smem_u32(sm.tab[i]), r, D);
+  if (hl == 1 && i == 0) FRSA_STAMP(27);
   // Delta = rowsum(O dO) with dO from the (unrotated) shared tile.
   const uint32_t dob = smem_u32(sm.dO[i]);
   float dl = 0.f;
@@ -133,26 +136,16 @@ __device__ __forceinline__ void bs_prep_q(BsSmem& sm, const BsParams& prm, int i
   if (leader) mbar_arrive(&sm.q_ready[i]);
 }
 
-// TMEM row (lane offset lane_off) of an f32 accumulator [tcol, tcol + 64) ->
-// global row tok, un-rotated with table tile `tab` unless tab == 0.
-template <typename T>
-__device__ __forceinline__ void bs_drain(uint32_t tcol, uint32_t lane_off, int r, int tok, int N,
-                                         int D, size_t row0, float scale, uint32_t tab, T* out) {
-  float v0[32], v1[32];
-  tmem_ld32(tcol + lane_off, v0);
-  tmem_ld32(tcol + lane_off + 32, v1);
-  tmem_wait_ld();
-  if (tok >= N) return;
-  store_row_t<T>(v0, v1, D, scale, tab, r, out + (row0 + tok) * D);
-}
-
 template <typename T>
 __global__ void __launch_bounds__(kBsThreads, 1)
     bwd_small_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_o, const BsParams prm) {
+                     const __grid_constant__ CUtensorMap tm_o,
+                     const __grid_constant__ CUtensorMap tm_dq,
+                     const __grid_constant__ CUtensorMap tm_dk,
+                     const __grid_constant__ CUtensorMap tm_dv, const BsParams prm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   BsSmem* smp = aligned_smem<BsSmem>(smem_raw);
   if (smp == nullptr) return;
@@ -176,14 +169,14 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.q_ready[s], 1);
       mbar_init(&sm.acc_full[s], 1);
+      mbar_init(&sm.dq_full[s], 1);
+      mbar_init(&sm.dq_free[s], 1);
     }
     mbar_init(&sm.st_full, 1);
     mbar_init(&sm.tm_free, 1);
     mbar_init(&sm.ds_full, 1);
     mbar_init(&sm.pds_free, 1);
     mbar_init(&sm.acc_free, 1);
-    mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_free, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -206,13 +199,25 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
       tma_prefetch_desc(&tm_o);
+      tma_prefetch_desc(&tm_dq);
+      tma_prefetch_desc(&tm_dk);
+      tma_prefetch_desc(&tm_dv);
       int hl = 0;
       for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
         const uint32_t fp = (hl & 1) ^ 1;
         // O rows feed Delta: this head's (first head only) and the next head's into L2.
+        // The next head's Q, K, V and dO go to L2 as well, so that its tile
+        // loads (issued only once this head releases the buffers) hit L2.
+        const int nbh = bh + (int)gridDim.x;
         for (int i = 0; i < nqt; ++i) {
           if (hl == 0) tma_prefetch_l2_3d(&tm_o, 0, i * kTile, bh);
-          if (bh + (int)gridDim.x < prm.BH) tma_prefetch_l2_3d(&tm_o, 0, i * kTile, bh + gridDim.x);
+          if (nbh < prm.BH) {
+            tma_prefetch_l2_3d(&tm_o, 0, i * kTile, nbh);
+            tma_prefetch_l2_3d(&tm_q, 0, i * kTile, nbh);
+            tma_prefetch_l2_3d(&tm_k, 0, i * kTile, nbh);
+            tma_prefetch_l2_3d(&tm_v, 0, i * kTile, nbh);
+            tma_prefetch_l2_3d(&tm_do, 0, i * kTile, nbh);
+          }
         }
         // Order: K0/V0, the query tiles, then the remaining key tiles.
         for (int step = 0; step < nkv + nqt; ++step) {
@@ -220,12 +225,14 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           if (is_kv) {
             const int j = (step == 0) ? 0 : step - nqt;
             mbar_wait(&sm.kv_empty[j], fp, abort_flag);
+            if (hl == 1 && j == 0) FRSA_STAMP_T(29, 0);
             mbar_arrive_expect_tx(&sm.kv_full[j], 2 * kChunkBytes);
             tma_load_3d(sm.k[j], &tm_k, &sm.kv_full[j], 0, j * kTile, bh);
             tma_load_3d(sm.v[j], &tm_v, &sm.kv_full[j], 0, j * kTile, bh);
           } else {
             const int i = step - 1;
             mbar_wait(&sm.q_empty[i], fp, abort_flag);
+            if (hl == 1 && i == 0) FRSA_STAMP_T(30, 0);
             mbar_arrive_expect_tx(&sm.q_full[i], 2 * kChunkBytes);
             tma_load_3d(sm.q[i], &tm_q, &sm.q_full[i], 0, i * kTile, bh);
             tma_load_3d(sm.dO[i], &tm_do, &sm.q_full[i], 0, i * kTile, bh);
@@ -258,19 +265,21 @@ __global__ void __launch_bounds__(kBsThreads, 1)
                  sw128_desc(smem_u32(sm.dO[i]) + koff, 16, 1024), idS, kk > 0);
         }
         mma_commit(&sm.st_full);
+        if (it >= 4 && it < 8) FRSA_STAMP_T(32 + 2 * (it - 4), 32);
       };
       auto issue_grads = [&](int it) __attribute__((always_inline)) {
         const int hl = it / per_head, w = it - hl * per_head;
         const int j = w / nqt, i = w - j * nqt;
         mbar_wait(&sm.ds_full, it & 1, abort_flag);
         tc_fence_after();
+        if (it >= 4 && it < 8) FRSA_STAMP_T(33 + 2 * (it - 4), 32);
         const int kvt = hl * nkv + j;   // running key-tile index
         if (i == 0 && kvt > 0) {
           mbar_wait(&sm.acc_free, (kvt - 1) & 1, abort_flag);   // dV/dK of the previous tile drained
           tc_fence_after();
         }
-        if (w == 0 && hl > 0) {
-          mbar_wait(&sm.dq_free, (hl - 1) & 1, abort_flag);     // previous head's dQ drained
+        if (j == 0 && hl > 0) {
+          mbar_wait(&sm.dq_free[i], (hl - 1) & 1, abort_flag);  // previous head's dQ_i drained
           tc_fence_after();
         }
         for (int kk = 0; kk < kTile / 16; ++kk) {
@@ -290,23 +299,28 @@ __global__ void __launch_bounds__(kBsThreads, 1)
                  sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
         }
         mma_commit(&sm.pds_free);
-        if (i == nqt - 1) {
-          mma_commit(&sm.acc_full[j]);
-          mma_commit(&sm.kv_empty[j]);
-        }
-        if (j == nkv - 1) mma_commit(&sm.q_empty[i]);
-        if (w == per_head - 1) mma_commit(&sm.dq_full);
+        // K_j/V_j and Q_i/dO_i are released by the aux warpgroup once it has
+        // staged the finished gradients in them and their TMA stores have read them.
+        if (i == nqt - 1) mma_commit(&sm.acc_full[j]);
+        if (j == nkv - 1) mma_commit(&sm.dq_full[i]);
+      };
+      // S^T/dP^T of the next iteration go ahead of this iteration's gradient
+      // products when their operands are already prepared; otherwise the
+      // gradients go first rather than wait behind the operand preparation.
+      auto st_ready = [&](int it) -> bool {
+        const int hl = it / per_head, w = it - hl * per_head;
+        const int j = w / nqt, i = w - j * nqt;
+        return mbar_test(&sm.k_ready[j], hl & 1) && mbar_test(&sm.q_ready[i], hl & 1);
       };
       if (total > 0) issue_st(0);
       for (int it = 0; it < total; ++it) {
-        const bool next_same_head = (it + 1 < total) && ((it + 1) % per_head != 0);
-        if (next_same_head) {
+        bool next_issued = false;
+        if (it + 1 < total && st_ready(it + 1)) {
           issue_st(it + 1);
-          issue_grads(it);
-        } else {
-          issue_grads(it);
-          if (it + 1 < total) issue_st(it + 1);
+          next_issued = true;
         }
+        issue_grads(it);
+        if (it + 1 < total && !next_issued) issue_st(it + 1);
       }
     }
   } else if (warp < 12) {
@@ -342,8 +356,10 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           tc_fence_before();
           named_bar(1, 256);
           if (leader) mbar_arrive(&sm.tm_free);
+          if (it >= 4 && it < 8) FRSA_STAMP_T(44 + it - 4, 128);
         } else if (it > 0) {
           mbar_wait(&sm.pds_free, (it - 1) & 1, abort_flag);   // P/dS tiles consumed
+          if (it >= 4 && it < 8) FRSA_STAMP_T(40 + it - 4, 128);
         }
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
@@ -395,9 +411,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     named_bar(2, 128);
 #define BS_PREP_K(j, hl) bs_prep_k<T>(sm, j, hl, r, D, leader, abort_flag)
 #define BS_PREP_Q(i, bh, hl) bs_prep_q<T>(sm, prm, i, bh, hl, r, leader, abort_flag)
-#define BS_DRAIN(tcol, tok, row0, scale, sel, out)                                     \
-  bs_drain<T>(tcol, lane_off, r, tok, N, D, row0, scale,                               \
-              (sel) < 0 ? 0u : smem_u32(sm.tab[(sel) & 1]), out)
+    const uint32_t tDQ = tmem + 384;
     int hl = 0;
     if ((int)blockIdx.x < prm.BH) {
       BS_PREP_K(0, 0);
@@ -406,37 +420,69 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     }
     FRSA_STAMP(24);
     for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
-      const size_t row0 = static_cast<size_t>(bh) * N;
       const int nbh = bh + gridDim.x;
       const bool has_next = nbh < prm.BH;
-      for (int j = 0; j < nkv; ++j) {
+      // dV_j, dK_j = R^T dK^_j scale: TMEM rows -> 16-bit rows staged in the
+      // (finished) V_j and K_j tiles -> TMA stores; K_j/V_j are released once
+      // the stores have read them.
+      auto drain_kv = [&](int j) {
         mbar_wait(&sm.acc_full[j], hl & 1, abort_flag);
         tc_fence_after();
         if (hl == 0) FRSA_STAMP(16 + 3 * j);
-        BS_DRAIN(tDV, j * kTile + r, row0, 1.f, -1, static_cast<T*>(prm.dv));
-        BS_DRAIN(tDK, j * kTile + r, row0, prm.scale, j, static_cast<T*>(prm.dk));
+        float v0[32], v1[32];
+        tmem_ld32(tDV + lane_off, v0);
+        tmem_ld32(tDV + lane_off + 32, v1);
+        tmem_wait_ld();
+        stage_row_t<T>(v0, v1, 1.f, 0u, r, smem_u32(sm.v[j]));
+        tmem_ld32(tDK + lane_off, v0);
+        tmem_ld32(tDK + lane_off + 32, v1);
+        tmem_wait_ld();
+        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[j]), r, smem_u32(sm.k[j]));
         tc_fence_before();
+        fence_proxy_async_smem();
         named_bar(2, 128);
-        if (leader) mbar_arrive(&sm.acc_free);
-        if (hl == 0) FRSA_STAMP(17 + 3 * j);
-        if (j == 0 && has_next) {
-          // The next head's first key and query tiles, while this head's
-          // remaining MMAs run.
-          BS_PREP_K(0, hl + 1);
-          BS_PREP_Q(0, nbh, hl + 1);
-          if (hl == 0) FRSA_STAMP(18);
+        if (leader) {
+          mbar_arrive(&sm.acc_free);
+          tma_store_3d(&tm_dv, sm.v[j], 0, j * kTile, bh);
+          tma_store_3d(&tm_dk, sm.k[j], 0, j * kTile, bh);
+          tma_store_commit();
+          tma_store_wait_read();
+          mbar_arrive(&sm.kv_empty[j]);
         }
+        if (hl == 0) FRSA_STAMP(17 + 3 * j);
+      };
+      // dQ_i = R^T dQ^_i scale, staged in the (finished) Q_i tile.
+      auto drain_q = [&](int i) {
+        mbar_wait(&sm.dq_full[i], hl & 1, abort_flag);
+        tc_fence_after();
+        if (hl == 0) FRSA_STAMP(21 + i);
+        float v0[32], v1[32];
+        tmem_ld32(tDQ + 64 * i + lane_off, v0);
+        tmem_ld32(tDQ + 64 * i + lane_off + 32, v1);
+        tmem_wait_ld();
+        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[i]), r, smem_u32(sm.q[i]));
+        tc_fence_before();
+        fence_proxy_async_smem();
+        named_bar(2, 128);
+        if (leader) {
+          mbar_arrive(&sm.dq_free[i]);
+          tma_store_3d(&tm_dq, sm.q[i], 0, i * kTile, bh);
+          tma_store_commit();
+          tma_store_wait_read();
+          mbar_arrive(&sm.q_empty[i]);
+        }
+      };
+      // Order: the next head's first key and query tiles are prepared as soon
+      // as their buffers are released, while this head's remaining MMAs run.
+      drain_kv(0);
+      if (has_next) BS_PREP_K(0, hl + 1);
+      drain_q(0);
+      if (has_next) BS_PREP_Q(0, nbh, hl + 1);
+      if (hl == 0) FRSA_STAMP(18);
+      for (int t = 1; t < nkv; ++t) {
+        drain_q(t);
+        drain_kv(t);
       }
-      mbar_wait(&sm.dq_full, hl & 1, abort_flag);
-      tc_fence_after();
-      if (hl == 0) FRSA_STAMP(21);
-      for (int i = 0; i < nqt; ++i) {
-        BS_DRAIN(tmem + 384 + 64 * i, i * kTile + r, row0, prm.scale, i, static_cast<T*>(prm.dq));
-      }
-      tc_fence_before();
-      named_bar(2, 128);
-      if (leader) mbar_arrive(&sm.dq_free);
-      if (hl == 0) FRSA_STAMP(22);
       if (has_next) {
         for (int i = 1; i < nqt; ++i) BS_PREP_Q(i, nbh, hl + 1);
         for (int j = 1; j < nkv; ++j) BS_PREP_K(j, hl + 1);
@@ -445,7 +491,6 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     }
 #undef BS_PREP_K
 #undef BS_PREP_Q
-#undef BS_DRAIN
   }
 
   tc_fence_before();
@@ -459,10 +504,10 @@ __global__ void __launch_bounds__(kBsThreads, 1)
 template <typename T>
 cudaError_t launch_bwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
                                const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                               const CUtensorMap& tm_do, const CUtensorMap& tm_o, const void* o,
-                               const float* lse, float* delta, const float* cosp,
-                               const float* sinp, void* dq, void* dk, void* dv,
-                               cudaStream_t stream) {
+                               const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                               const CUtensorMap* tm_grads, const void* o, const float* lse,
+                               float* delta, const float* cosp, const float* sinp, void* dq,
+                               void* dk, void* dv, cudaStream_t stream) {
   BsParams p;
   p.cosp = cosp;
   p.sinp = sinp;
@@ -491,7 +536,8 @@ cudaError_t launch_bwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int grid = s.BH < nsm ? s.BH : nsm;
-  kern<<<grid, kBsThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, tm_o, p);
+  kern<<<grid, kBsThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads[0], tm_grads[1],
+                                            tm_grads[2], p);
   return cudaGetLastError();
 }
 
@@ -499,13 +545,14 @@ cudaError_t launch_bwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
 
 cudaError_t launch_bwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
                              const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                             const CUtensorMap& tm_do, const CUtensorMap& tm_o, const void* o,
-                             const float* lse, float* delta, const float* cosp, const float* sinp,
-                             void* dq, void* dk, void* dv, cudaStream_t stream) {
-  return s.bf16 ? launch_bwd_small_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, lse,
-                                                    delta, cosp, sinp, dq, dk, dv, stream)
-                : launch_bwd_small_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, lse, delta,
-                                             cosp, sinp, dq, dk, dv, stream);
+                             const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                             const CUtensorMap* tm_grads, const void* o, const float* lse,
+                             float* delta, const float* cosp, const float* sinp, void* dq,
+                             void* dk, void* dv, cudaStream_t stream) {
+  return s.bf16 ? launch_bwd_small_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads, o,
+                                                    lse, delta, cosp, sinp, dq, dk, dv, stream)
+                : launch_bwd_small_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads, o, lse,
+                                             delta, cosp, sinp, dq, dk, dv, stream);
 }
 
 }  // namespace frsa

@@ -37,18 +37,20 @@ cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
 // Persistent backward for N <= 256, D <= 64 (dQ reduced on chip).
 cudaError_t launch_bwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
                              const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                             const CUtensorMap& tm_do, const CUtensorMap& tm_o, const void* o,
-                             const float* lse, float* delta, const float* cosp, const float* sinp,
-                             void* dq, void* dk, void* dv, cudaStream_t stream);
+                             const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                             const CUtensorMap* tm_grads, const void* o, const float* lse,
+                             float* delta, const float* cosp, const float* sinp, void* dq,
+                             void* dk, void* dv, cudaStream_t stream);
 
 // Backward (delta preprocess + main kernel + optional dQ finalize).
 // dq_accum: fp32 [BH, N, D] workspace or nullptr when bwd_needs_workspace() is false.
+// tm_grads: maps over dQ, dK, dV (in that order), required when
+// bwd_needs_workspace() is false (the persistent kernel stores through them).
 bool bwd_needs_workspace(const LaunchShape& s);
 cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                        const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
-                       const void* o,
-                       const void* d_o, const float* lse, float* delta, const float* cosp,
-                       const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
-                       cudaStream_t stream);
+                       const void* o, const CUtensorMap* tm_grads, const void* d_o, const float* lse,
+                       float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
+                       void* dv, float* dq_accum, cudaStream_t stream);
 
 }  // namespace frsa

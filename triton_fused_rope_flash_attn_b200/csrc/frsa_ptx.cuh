@@ -57,16 +57,16 @@ __device__ __forceinline__ uint64_t globaltimer() {
 #define FRSA_STAMP_TID 64
 #endif
 #ifdef FRSA_TRACE
-__device__ unsigned long long g_trace[4096 * 32];
+__device__ unsigned long long g_trace[2048 * 64];
 #define FRSA_STAMP(slot)                                                       \
   do {                                                                         \
-    if (blockIdx.x < 4096 && threadIdx.x == FRSA_STAMP_TID)                    \
-      ::frsa::g_trace[blockIdx.x * 32 + (slot)] = ::frsa::globaltimer();      \
+    if (blockIdx.x < 2048 && threadIdx.x == FRSA_STAMP_TID)                    \
+      ::frsa::g_trace[blockIdx.x * 64 + (slot)] = ::frsa::globaltimer();      \
   } while (0)
 #define FRSA_STAMP_T(slot, tid)                                                \
   do {                                                                         \
-    if (blockIdx.x < 4096 && threadIdx.x == (tid))                             \
-      ::frsa::g_trace[blockIdx.x * 32 + (slot)] = ::frsa::globaltimer();      \
+    if (blockIdx.x < 2048 && threadIdx.x == (tid))                             \
+      ::frsa::g_trace[blockIdx.x * 64 + (slot)] = ::frsa::globaltimer();      \
   } while (0)
 #else
 #define FRSA_STAMP(slot) \
@@ -113,6 +113,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity), "r"(100000u)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }

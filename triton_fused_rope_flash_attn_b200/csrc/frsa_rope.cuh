@@ -277,37 +277,51 @@ __device__ __forceinline__ void rotate_row_t(uint32_t tile, uint32_t tab, int r,
   }
 }
 
-// Scale (and with tab != 0 R^T-unrotate) a row of 64 f32 values, given as two
-// 32-value halves, and store it.
+// Granule g (values 8g..8g+7) of a row of 64 f32 values, given as two
+// 32-value halves, scaled and, with tab != 0, R^T-unrotated; packed to 16 bits.
+template <typename T>
+__device__ __forceinline__ uint4 row_granule_t(const float (&v0)[32], const float (&v1)[32], int g,
+                                               float scale, uint32_t tab, int r) {
+  uint32_t tw[4] = {0u, 0u, 0u, 0u};
+  if (tab != 0u) {
+    const uint4 t = lds_u4(tab + sw128_off(r, g));
+    tw[0] = t.x; tw[1] = t.y; tw[2] = t.z; tw[3] = t.w;
+  }
+  float u[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int c = 8 * g + 2 * e;
+    float a = (c < 32 ? v0[c & 31] : v1[c & 31]) * scale;
+    float b = (c < 32 ? v0[(c + 1) & 31] : v1[(c + 1) & 31]) * scale;
+    if (tab != 0u) {
+      const float2 cs = Elt<__half>::unpack(tw[e]);
+      const float a2 = a * cs.x + b * cs.y;
+      b = b * cs.x - a * cs.y;
+      a = a2;
+    }
+    u[2 * e] = a;
+    u[2 * e + 1] = b;
+  }
+  return pack8<T>(u);
+}
+
+// Scale (and with tab != 0 R^T-unrotate) a row of 64 f32 values and store it
+// to global memory.
 template <typename T>
 __device__ __forceinline__ void store_row_t(const float (&v0)[32], const float (&v1)[32], int D,
                                             float scale, uint32_t tab, int r, T* dst) {
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    if (8 * g < D) {
-      uint32_t tw[4] = {0u, 0u, 0u, 0u};
-      if (tab != 0u) {
-        const uint4 t = lds_u4(tab + sw128_off(r, g));
-        tw[0] = t.x; tw[1] = t.y; tw[2] = t.z; tw[3] = t.w;
-      }
-      float u[8];
+  for (int g = 0; g < 8; ++g)
+    if (8 * g < D) reinterpret_cast<uint4*>(dst)[g] = row_granule_t<T>(v0, v1, g, scale, tab, r);
+}
+
+// The same row written as row r of a one-chunk (128B-swizzled) shared tile,
+// all 64 columns (a TMA store of the tile clips columns >= D).
+template <typename T>
+__device__ __forceinline__ void stage_row_t(const float (&v0)[32], const float (&v1)[32],
+                                            float scale, uint32_t tab, int r, uint32_t tile) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c = 8 * g + 2 * e;
-        float a = (c < 32 ? v0[c & 31] : v1[c & 31]) * scale;
-        float b = (c < 32 ? v0[(c + 1) & 31] : v1[(c + 1) & 31]) * scale;
-        if (tab != 0u) {
-          const float2 cs = Elt<__half>::unpack(tw[e]);
-          const float a2 = a * cs.x + b * cs.y;
-          b = b * cs.x - a * cs.y;
-          a = a2;
-        }
-        u[2 * e] = a;
-        u[2 * e + 1] = b;
-      }
-      reinterpret_cast<uint4*>(dst)[g] = pack8<T>(u);
-    }
-  }
+  for (int g = 0; g < 8; ++g) sts_u4(tile + sw128_off(r, g), row_granule_t<T>(v0, v1, g, scale, tab, r));
 }
 
 }  // namespace frsa
