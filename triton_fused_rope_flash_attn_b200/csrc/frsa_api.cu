@@ -200,7 +200,7 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
 const char* frsa_last_error_detail(void) { return g_last_detail; }
 
 #ifdef FRSA_TRACE
-// Trace builds only: copy the phase stamps (4096 CTAs x 32 slots) to `host`.
+// Trace builds only: copy the phase stamps (2048 CTAs x 64 slots) to `host`.
 int frsa_trace_copy(unsigned long long* host, size_t n) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FRSA_ERR_LAUNCH;
   return cudaMemcpyFromSymbol(host, frsa::g_trace, n * sizeof(unsigned long long)) ==

@@ -385,6 +385,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     j0 = unit_j0(u);
     head_row0 = static_cast<size_t>(bh) * N;
     const int qbase = qi, kvbase = kvi, itbase = it;
+    (void)itbase;  // used by trace stamps only
     if (hl == 1) FRSA_STAMP(16);
     prep_k(j0, kvbase);
     if (hl == 1) FRSA_STAMP(17);

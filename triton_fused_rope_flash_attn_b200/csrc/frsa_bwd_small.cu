@@ -4,35 +4,40 @@
 // compute, one head per unit, dQ reduced on chip (no atomics, deterministic).
 //
 // Per (key tile j, query tile i) iteration, with thread = key row:
-//   S^T = K^_j Q^_i^T, dP^T = V_j dO_i^T          (tcgen05, TMEM)
-//   P = exp2(S^T c2 - lse2_q), dS = P (dP - Delta_q)   (registers -> smem, 16-bit)
-//   dV_j += P dO_i, dK^_j += dS Q^_i, dQ^_i += dS^T K^_j   (tcgen05, TMEM)
+//   S^T = K^_j Q^_i^T, dP^T = V_j dO_i^T              (tcgen05, TMEM)
+//   P = exp2(S^T c2 - lse2_q), dS = P (dP - Delta_q)   (registers)
+//   P and dS go back to TMEM as packed 16-bit pairs over S^T and dP^T, and dS
+//   also to shared memory (the dQ product needs it query-major);
+//   dV_j += P dO_i, dK^_j += dS Q^_i   (A operand from TMEM)
+//   dQ^_i += dS^T K^_j                 (A operand from shared memory)
+//
+// Keeping P and dS in TMEM halves the shared-memory traffic of the dV and dK
+// products (the bound of this kernel is shared-memory bandwidth, not the
+// tensor core) and frees the P tile, whose space holds a third query-tile
+// slot: the next head's query tiles load and are prepared a head ahead.
 //
 // Warp roles (16 warps, 512 threads):
-//   warp 0        TMA producer (K, V, Q, dO tiles; O of the next head into L2)
+//   warp 0        TMA producer (K, V, Q, dO tiles; the next head's tiles, O and
+//                 lse into L2)
 //   warp 1        TMEM allocator + MMA issuer
 //   warps 2..3    idle (complete warpgroup 0 for the register rebalancing)
 //   warps 4..11   two elementwise warpgroups: warpgroup g computes P and dS for
 //                 query columns [64 g, 64 g + 64) of each iteration
 //   warps 12..15  aux warpgroup: operand preparation (RoPE of K and Q in shared
 //                 memory, lse2 and Delta = rowsum(dO O)) and the epilogues
-//                 (dV, dK = R^T dK^ scale, dQ = R^T dQ^ scale) straight from
-//                 TMEM rows to global memory (thread = row)
+//                 (dV, dK = R^T dK^ scale, dQ = R^T dQ^ scale: TMEM rows staged
+//                 in the finished K/V/Q tiles and written by TMA stores)
 //
-// The aux warpgroup works ahead of and behind the tensor core: it prepares
-// the next head's first tiles while the current head's MMAs run and drains a
-// key tile's dV/dK while the next key tile is computed. The MMA warp issues
-// S/dP of the next iteration as soon as the elementwise warps have read the
-// current S/dP, before the current iteration's dV/dK/dQ products.
+// TMEM columns: [0,128) S^T (P packed: columns [64 g, 64 g + 32) hold query
+// columns [64 g, 64 g + 64)), [128,256) dP^T (dS packed likewise), [256,320)
+// dV, [320,384) dK^, [384 + 64 i, 448 + 64 i) dQ^ of query tile i.
 //
-// TMEM columns: [0,128) S^T, [128,256) dP^T, [256,320) dV, [320,384) dK^,
-// [384 + 64 i, 448 + 64 i) dQ^ of query tile i.
+// Query tiles rotate through three shared slots: fill u = hl * nqt + i of this
+// CTA (head hl, tile i) uses slot u % 3, and its barriers' phase is (u / 3) & 1.
 //
 // Registers: launched at 128 per thread (512 x 128 = 65536), then warpgroup 0
-// drops to 64, the aux warpgroup rises to 192 (it keeps the RoPE table values
-// of its rows of both token tiles, identical for every head, as packed f16
-// pairs) and the elementwise warpgroups keep 128:
-// 128*64 + 128*192 + 256*128 = 65536.
+// drops to 64, the aux warpgroup rises to 192 and the elementwise warpgroups
+// keep 128: 128*64 + 128*192 + 256*128 = 65536.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
@@ -45,21 +50,23 @@ namespace frsa {
 namespace {
 
 constexpr int kBsThreads = 512;
+constexpr int kQSlots = 3;
 constexpr uint32_t kBsRegsCtl = 64, kBsRegsAux = 192, kBsRegsElem = 128;
 
 struct BsSmem {
   uint8_t k[2][kChunkBytes];
   uint8_t v[2][kChunkBytes];
-  uint8_t q[2][kChunkBytes];
-  uint8_t dO[2][kChunkBytes];
-  uint8_t p[2][kChunkBytes];    // P  [128 key][128 query], two 64-column chunks
-  uint8_t ds[2][kChunkBytes];   // dS [128 key][128 query]
+  uint8_t q[kQSlots][kChunkBytes];
+  uint8_t dO[kQSlots][kChunkBytes];
+  uint8_t ds[2][kChunkBytes];   // dS [128 key][128 query], two 64-column chunks
   uint8_t tab[2][kChunkBytes];  // f16 (cos, sin) table tiles of token tiles 0 and 1
+  // lse2 / Delta of query-tile fill u live in entry u & 1 (written once the
+  // elementwise warps are done with fill u - 2).
   float lse2[2][kTile];
   float delta[2][kTile];
   uint64_t kv_full[2], kv_empty[2], k_ready[2];
-  uint64_t q_full[2], q_empty[2], q_ready[2];
-  uint64_t st_full, tm_free, ds_full, pds_free;
+  uint64_t q_full[kQSlots], q_empty[kQSlots], q_ready[kQSlots];
+  uint64_t st_full, ds_full;
   uint64_t acc_full[2], acc_free, dq_full[2], dq_free[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -78,6 +85,9 @@ struct BsParams {
   float c2, scale;
 };
 
+// Slot and barrier phase of query-tile fill u.
+__device__ __forceinline__ int qslot(int u) { return u % kQSlots; }
+__device__ __forceinline__ uint32_t qphase(int u) { return static_cast<uint32_t>(u / kQSlots) & 1u; }
 
 // Aux-warpgroup steps (thread = tile row r); RoPE tables come from the
 // shared table tiles (identical for every head, filled once).
@@ -85,18 +95,25 @@ template <typename T>
 __device__ __forceinline__ void bs_prep_k(BsSmem& sm, int j, int hl, int r, int D, bool leader,
                                           volatile int* abort_flag) {
   mbar_wait(&sm.kv_full[j], hl & 1, abort_flag);
-  if (hl == 1 && j == 0) FRSA_STAMP(25);
   rotate_row_t<T>(smem_u32(sm.k[j]), smem_u32(sm.tab[j]), r, D);
   fence_proxy_async_smem();
   named_bar(2, 128);
   if (leader) mbar_arrive(&sm.k_ready[j]);
 }
 
+// Query-tile preparation, part A: rotate the tile in its slot and compute
+// this row's Delta = rowsum(O dO) (dO from the unrotated shared tile); the
+// row's lse2 and Delta are returned, to be published by part B.
+struct QPrep {
+  float lse2, delta;
+};
+
 template <typename T>
-__device__ __forceinline__ void bs_prep_q(BsSmem& sm, const BsParams& prm, int i, int bh, int hl,
-                                          int r, bool leader, volatile int* abort_flag) {
+__device__ __forceinline__ QPrep bs_prep_qa(BsSmem& sm, const BsParams& prm, int i, int bh, int hl,
+                                            int r, volatile int* abort_flag) {
   const int N = prm.N, D = prm.D;
   const int q0 = i * kTile;
+  const int u = hl * prm.nqt + i, sl = qslot(u);
   const size_t row0 = static_cast<size_t>(bh) * N;
   const bool qv = q0 + r < N;
   const float lsev = qv ? prm.lse[row0 + q0 + r] : 0.f;
@@ -107,14 +124,9 @@ __device__ __forceinline__ void bs_prep_q(BsSmem& sm, const BsParams& prm, int i
 #pragma unroll
   for (int g = 0; g < 8; ++g)
     og[g] = (qv && 8 * g < D) ? __ldg(orow + g) : make_uint4(0u, 0u, 0u, 0u);
-  mbar_wait(&sm.q_full[i], hl & 1, abort_flag);
-  if (hl == 1 && i == 0) FRSA_STAMP(26);
-  // Padded query rows get lse2 = +inf, so their P (and dS) is exactly 0.
-  sm.lse2[i][r] = qv ? lsev * 1.4426950408889634f : INFINITY;
-  rotate_row_t<T>(smem_u32(sm.q[i]), smem_u32(sm.tab[i]), r, D);
-  if (hl == 1 && i == 0) FRSA_STAMP(27);
-  // Delta = rowsum(O dO) with dO from the (unrotated) shared tile.
-  const uint32_t dob = smem_u32(sm.dO[i]);
+  mbar_wait(&sm.q_full[sl], qphase(u), abort_flag);
+  rotate_row_t<T>(smem_u32(sm.q[sl]), smem_u32(sm.tab[i]), r, D);
+  const uint32_t dob = smem_u32(sm.dO[sl]);
   float dl = 0.f;
 #pragma unroll
   for (int g = 0; g < 8; ++g) {
@@ -129,11 +141,21 @@ __device__ __forceinline__ void bs_prep_q(BsSmem& sm, const BsParams& prm, int i
       }
     }
   }
-  sm.delta[i][r] = dl;
   if (prm.delta_out != nullptr && qv) prm.delta_out[row0 + q0 + r] = dl;
+  // Padded query rows get lse2 = +inf, so their P (and dS) is exactly 0.
+  return QPrep{qv ? lsev * 1.4426950408889634f : INFINITY, dl};
+}
+
+// Part B: publish lse2 / Delta and mark the tile ready. Runs once the
+// elementwise warps are done with query-tile fill u - 2 (same entry).
+__device__ __forceinline__ void bs_prep_qb(BsSmem& sm, const BsParams& prm, int i, int hl, int r,
+                                           bool leader, QPrep v) {
+  const int u = hl * prm.nqt + i;
+  sm.lse2[u & 1][r] = v.lse2;
+  sm.delta[u & 1][r] = v.delta;
   fence_proxy_async_smem();
   named_bar(2, 128);
-  if (leader) mbar_arrive(&sm.q_ready[i]);
+  if (leader) mbar_arrive(&sm.q_ready[qslot(u)]);
 }
 
 template <typename T>
@@ -165,17 +187,17 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
       mbar_init(&sm.k_ready[s], 1);
-      mbar_init(&sm.q_full[s], 1);
-      mbar_init(&sm.q_empty[s], 1);
-      mbar_init(&sm.q_ready[s], 1);
       mbar_init(&sm.acc_full[s], 1);
       mbar_init(&sm.dq_full[s], 1);
       mbar_init(&sm.dq_free[s], 1);
     }
+    for (int s = 0; s < kQSlots; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
+      mbar_init(&sm.q_ready[s], 1);
+    }
     mbar_init(&sm.st_full, 1);
-    mbar_init(&sm.tm_free, 1);
     mbar_init(&sm.ds_full, 1);
-    mbar_init(&sm.pds_free, 1);
     mbar_init(&sm.acc_free, 1);
     fence_mbar_init();
   }
@@ -189,6 +211,9 @@ __global__ void __launch_bounds__(kBsThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320;
+  const int per_head = nkv * nqt;
+  const int nheads = (prm.BH - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int total = nheads * per_head;
 
   if (warp < 4) {
     setmaxnreg_dec<kBsRegsCtl>();
@@ -204,11 +229,10 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       tma_prefetch_desc(&tm_dv);
       int hl = 0;
       for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
-        const uint32_t fp = (hl & 1) ^ 1;
-        // O rows feed Delta: this head's (first head only) and the next head's into L2.
-        // The next head's Q, K, V and dO go to L2 as well, so that its tile
-        // loads (issued only once this head releases the buffers) hit L2.
+        // The next head's operands (and this head's O, for the first head) go
+        // to L2 so that their loads and the Delta reads hit L2.
         const int nbh = bh + (int)gridDim.x;
+        if (nbh < prm.BH) prefetch_l2_bytes(prm.lse + static_cast<size_t>(nbh) * N, N * 4);
         for (int i = 0; i < nqt; ++i) {
           if (hl == 0) tma_prefetch_l2_3d(&tm_o, 0, i * kTile, bh);
           if (nbh < prm.BH) {
@@ -219,24 +243,17 @@ __global__ void __launch_bounds__(kBsThreads, 1)
             tma_prefetch_l2_3d(&tm_do, 0, i * kTile, nbh);
           }
         }
-        // Order: K0/V0, the query tiles, then the remaining key tiles.
-        for (int step = 0; step < nkv + nqt; ++step) {
-          const bool is_kv = (step == 0) || (step > nqt);
-          if (is_kv) {
-            const int j = (step == 0) ? 0 : step - nqt;
-            mbar_wait(&sm.kv_empty[j], fp, abort_flag);
-            if (hl == 1 && j == 0) FRSA_STAMP_T(29, 0);
-            mbar_arrive_expect_tx(&sm.kv_full[j], 2 * kChunkBytes);
-            tma_load_3d(sm.k[j], &tm_k, &sm.kv_full[j], 0, j * kTile, bh);
-            tma_load_3d(sm.v[j], &tm_v, &sm.kv_full[j], 0, j * kTile, bh);
-          } else {
-            const int i = step - 1;
-            mbar_wait(&sm.q_empty[i], fp, abort_flag);
-            if (hl == 1 && i == 0) FRSA_STAMP_T(30, 0);
-            mbar_arrive_expect_tx(&sm.q_full[i], 2 * kChunkBytes);
-            tma_load_3d(sm.q[i], &tm_q, &sm.q_full[i], 0, i * kTile, bh);
-            tma_load_3d(sm.dO[i], &tm_do, &sm.q_full[i], 0, i * kTile, bh);
-          }
+        // Order Q0, K0, Q1, K1: the order in which the buffers are released.
+        for (int t = 0; t < nkv; ++t) {
+          const int u = hl * nqt + t, sl = qslot(u);
+          mbar_wait(&sm.q_empty[sl], qphase(u) ^ 1u, abort_flag);
+          mbar_arrive_expect_tx(&sm.q_full[sl], 2 * kChunkBytes);
+          tma_load_3d(sm.q[sl], &tm_q, &sm.q_full[sl], 0, t * kTile, bh);
+          tma_load_3d(sm.dO[sl], &tm_do, &sm.q_full[sl], 0, t * kTile, bh);
+          mbar_wait(&sm.kv_empty[t], (hl & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.kv_full[t], 2 * kChunkBytes);
+          tma_load_3d(sm.k[t], &tm_k, &sm.kv_full[t], 0, t * kTile, bh);
+          tma_load_3d(sm.v[t], &tm_v, &sm.kv_full[t], 0, t * kTile, bh);
         }
       }
     } else if (warp == 1 && lane == 0) {
@@ -245,34 +262,31 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);   // S^T, dP^T
       const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
       const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
-      const int per_head = nkv * nqt;
-      const int total = ((prm.BH - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * per_head;
       auto issue_st = [&](int it) __attribute__((always_inline)) {
         const int hl = it / per_head, w = it - hl * per_head;
         const int j = w / nqt, i = w - j * nqt;
+        const int u = hl * nqt + i, sl = qslot(u);
         mbar_wait(&sm.k_ready[j], hl & 1, abort_flag);
-        mbar_wait(&sm.q_ready[i], hl & 1, abort_flag);
-        if (it > 0) mbar_wait(&sm.tm_free, (it - 1) & 1, abort_flag);
+        mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);
         tc_fence_after();
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
           mma_ss(tST, sw128_desc(smem_u32(sm.k[j]) + koff, 16, 1024),
-                 sw128_desc(smem_u32(sm.q[i]) + koff, 16, 1024), idS, kk > 0);
+                 sw128_desc(smem_u32(sm.q[sl]) + koff, 16, 1024), idS, kk > 0);
         }
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
           mma_ss(tDPT, sw128_desc(smem_u32(sm.v[j]) + koff, 16, 1024),
-                 sw128_desc(smem_u32(sm.dO[i]) + koff, 16, 1024), idS, kk > 0);
+                 sw128_desc(smem_u32(sm.dO[sl]) + koff, 16, 1024), idS, kk > 0);
         }
         mma_commit(&sm.st_full);
-        if (it >= 4 && it < 8) FRSA_STAMP_T(32 + 2 * (it - 4), 32);
       };
       auto issue_grads = [&](int it) __attribute__((always_inline)) {
         const int hl = it / per_head, w = it - hl * per_head;
         const int j = w / nqt, i = w - j * nqt;
+        const int sl = qslot(hl * nqt + i);
         mbar_wait(&sm.ds_full, it & 1, abort_flag);
         tc_fence_after();
-        if (it >= 4 && it < 8) FRSA_STAMP_T(33 + 2 * (it - 4), 32);
         const int kvt = hl * nkv + j;   // running key-tile index
         if (i == 0 && kvt > 0) {
           mbar_wait(&sm.acc_free, (kvt - 1) & 1, abort_flag);   // dV/dK of the previous tile drained
@@ -283,14 +297,16 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           tc_fence_after();
         }
         for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk & 3) * 32;
+          // Query columns [16 kk, 16 kk + 16) of P / dS: packed TMEM columns
+          // 64 (kk / 4) + 8 (kk % 4).
+          const uint32_t pcol = 64 * (kk >> 2) + 8 * (kk & 3);
           const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-          // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
-          mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
-                 sw128_desc(smem_u32(sm.dO[i]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
-          // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
-          mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
-                 sw128_desc(smem_u32(sm.q[i]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
+          // dV += P dO : A = P [key][query] in TMEM, B = dO [query][d] MN-major.
+          mma_ts(tDV, tST + pcol, sw128_desc(smem_u32(sm.dO[sl]) + kk * 2048, kChunkBytes, 1024),
+                 idKV, acc);
+          // dK^ += dS Q^ : A = dS [key][query] in TMEM, B = Q^ [query][d] MN-major.
+          mma_ts(tDK, tDPT + pcol, sw128_desc(smem_u32(sm.q[sl]) + kk * 2048, kChunkBytes, 1024),
+                 idKV, acc);
         }
         // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
         for (int kk = 0; kk < kTile / 16; ++kk) {
@@ -298,29 +314,19 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           mma_ss(tmem + 384 + 64 * i, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
                  sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
         }
-        mma_commit(&sm.pds_free);
-        // K_j/V_j and Q_i/dO_i are released by the aux warpgroup once it has
-        // staged the finished gradients in them and their TMA stores have read them.
+        // K_j/V_j and the query slot are released by the aux warpgroup once it
+        // has staged the finished gradients in them and their stores have read them.
         if (i == nqt - 1) mma_commit(&sm.acc_full[j]);
         if (j == nkv - 1) mma_commit(&sm.dq_full[i]);
       };
-      // S^T/dP^T of the next iteration go ahead of this iteration's gradient
-      // products when their operands are already prepared; otherwise the
-      // gradients go first rather than wait behind the operand preparation.
-      auto st_ready = [&](int it) -> bool {
-        const int hl = it / per_head, w = it - hl * per_head;
-        const int j = w / nqt, i = w - j * nqt;
-        return mbar_test(&sm.k_ready[j], hl & 1) && mbar_test(&sm.q_ready[i], hl & 1);
-      };
+      // S^T/dP^T of iteration it + 1 overwrite P/dS of iteration it in TMEM,
+      // so they follow its gradient products in the (in-order) MMA pipe; their
+      // completion (st_full) also tells the elementwise warps that the dQ
+      // product has read the shared dS tile.
       if (total > 0) issue_st(0);
       for (int it = 0; it < total; ++it) {
-        bool next_issued = false;
-        if (it + 1 < total && st_ready(it + 1)) {
-          issue_st(it + 1);
-          next_issued = true;
-        }
         issue_grads(it);
-        if (it + 1 < total && !next_issued) issue_st(it + 1);
+        if (it + 1 < total) issue_st(it + 1);
       }
     }
   } else if (warp < 12) {
@@ -333,73 +339,55 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const bool leader = threadIdx.x == 128;
     const float c2 = prm.c2;
-    const int per_head = nkv * nqt;
-    const int total = ((prm.BH - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * per_head;
-    const uint32_t pbase = smem_u32(sm.p[g]), dbase = smem_u32(sm.ds[g]);
+    const uint32_t dbase = smem_u32(sm.ds[g]);
     for (int it = 0; it < total; ++it) {
       const int hl = it / per_head, w = it - hl * per_head;
       const int i = w - (w / nqt) * nqt;
-      mbar_wait(&sm.q_ready[i], hl & 1, abort_flag);   // lse2 / Delta of this query tile
+      const int u = hl * nqt + i, sl = qslot(u);
+      mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);   // lse2 / Delta of this query tile
       mbar_wait(&sm.st_full, it & 1, abort_flag);
       tc_fence_after();
-      if (it < 8) FRSA_STAMP_T(it * 2, 128);
-      const uint32_t lbase = smem_u32(&sm.lse2[i][g * 64]);
-      const uint32_t ebase = smem_u32(&sm.delta[i][g * 64]);
+      const uint32_t lbase = smem_u32(&sm.lse2[u & 1][g * 64]);
+      const uint32_t ebase = smem_u32(&sm.delta[u & 1][g * 64]);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float sv[32], dp[32];
         tmem_ld32(tST + lane_off + g * 64 + hh * 32, sv);
         tmem_ld32(tDPT + lane_off + g * 64 + hh * 32, dp);
         tmem_wait_ld();
-        if (hh == 1) {
-          // S^T / dP^T fully read: the next S^T, dP^T may overwrite them.
-          tc_fence_before();
-          named_bar(1, 256);
-          if (leader) mbar_arrive(&sm.tm_free);
-          if (it >= 4 && it < 8) FRSA_STAMP_T(44 + it - 4, 128);
-        } else if (it > 0) {
-          mbar_wait(&sm.pds_free, (it - 1) & 1, abort_flag);   // P/dS tiles consumed
-          if (it >= 4 && it < 8) FRSA_STAMP_T(40 + it - 4, 128);
-        }
+        uint32_t pk[16], dk[16];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
           const float4 l4 = lds_f4(lbase + (hh * 32 + c4 * 4) * 4);
           const float4 d4 = lds_f4(ebase + (hh * 32 + c4 * 4) * 4);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = c4 * 4 + e;
-            const float pv = ex2(fmaf(sv[c], c2, -lv[e]));
-            sv[c] = pv;
-            dp[c] = pv * (dp[c] - dv4[e]);
-          }
+          const float p0 = ex2(fmaf(sv[4 * c4 + 0], c2, -l4.x));
+          const float p1 = ex2(fmaf(sv[4 * c4 + 1], c2, -l4.y));
+          const float p2 = ex2(fmaf(sv[4 * c4 + 2], c2, -l4.z));
+          const float p3 = ex2(fmaf(sv[4 * c4 + 3], c2, -l4.w));
+          pk[2 * c4] = Elt<T>::pack(p0, p1);
+          pk[2 * c4 + 1] = Elt<T>::pack(p2, p3);
+          dk[2 * c4] = Elt<T>::pack(p0 * (dp[4 * c4 + 0] - d4.x), p1 * (dp[4 * c4 + 1] - d4.y));
+          dk[2 * c4 + 1] = Elt<T>::pack(p2 * (dp[4 * c4 + 2] - d4.z), p3 * (dp[4 * c4 + 3] - d4.w));
         }
+        // Columns [64 g + 32 hh, +32) -> packed TMEM columns 64 g + 16 hh (already
+        // read by this thread: the write front trails the read front).
+        tmem_st16(tST + lane_off + g * 64 + hh * 16, pk);
+        tmem_st16(tDPT + lane_off + g * 64 + hh * 16, dk);
 #pragma unroll
-        for (int g4 = 0; g4 < 4; ++g4) {
-          const uint32_t off = sw128_off(r, hh * 4 + g4);
-          uint4 wv;
-          wv.x = Elt<T>::pack(sv[g4 * 8 + 0], sv[g4 * 8 + 1]);
-          wv.y = Elt<T>::pack(sv[g4 * 8 + 2], sv[g4 * 8 + 3]);
-          wv.z = Elt<T>::pack(sv[g4 * 8 + 4], sv[g4 * 8 + 5]);
-          wv.w = Elt<T>::pack(sv[g4 * 8 + 6], sv[g4 * 8 + 7]);
-          sts_u4(pbase + off, wv);
-          wv.x = Elt<T>::pack(dp[g4 * 8 + 0], dp[g4 * 8 + 1]);
-          wv.y = Elt<T>::pack(dp[g4 * 8 + 2], dp[g4 * 8 + 3]);
-          wv.z = Elt<T>::pack(dp[g4 * 8 + 4], dp[g4 * 8 + 5]);
-          wv.w = Elt<T>::pack(dp[g4 * 8 + 6], dp[g4 * 8 + 7]);
-          sts_u4(dbase + off, wv);
-        }
+        for (int g4 = 0; g4 < 4; ++g4)
+          sts_u4(dbase + sw128_off(r, hh * 4 + g4),
+                 make_uint4(dk[4 * g4], dk[4 * g4 + 1], dk[4 * g4 + 2], dk[4 * g4 + 3]));
       }
+      tmem_wait_st();
       fence_proxy_async_smem();
+      tc_fence_before();
       named_bar(1, 256);
       if (leader) mbar_arrive(&sm.ds_full);
-      if (it < 8) FRSA_STAMP_T(it * 2 + 1, 128);
     }
   } else {
     setmaxnreg_inc<kBsRegsAux>();
     // ------------------------------------------------------------ aux warpgroup
-    // Thread = tile row = TMEM lane (r); the RoPE table values of row r of
-    // token tiles 0 and 1 (the same for every head) stay in registers.
+    // Thread = tile row = TMEM lane (r).
     const int aw = warp - 12;            // 0..3 == TMEM lane quarter
     const int r = aw * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(aw * 32) << 16;
@@ -410,15 +398,15 @@ __global__ void __launch_bounds__(kBsThreads, 1)
                  prm.sinp);
     named_bar(2, 128);
 #define BS_PREP_K(j, hl) bs_prep_k<T>(sm, j, hl, r, D, leader, abort_flag)
-#define BS_PREP_Q(i, bh, hl) bs_prep_q<T>(sm, prm, i, bh, hl, r, leader, abort_flag)
+#define BS_PREP_QA(i, bh, hl) bs_prep_qa<T>(sm, prm, i, bh, hl, r, abort_flag)
+#define BS_PREP_QB(i, hl, v) bs_prep_qb(sm, prm, i, hl, r, leader, v)
     const uint32_t tDQ = tmem + 384;
     int hl = 0;
     if ((int)blockIdx.x < prm.BH) {
       BS_PREP_K(0, 0);
-      for (int i = 0; i < nqt; ++i) BS_PREP_Q(i, blockIdx.x, 0);
+      for (int i = 0; i < nqt; ++i) BS_PREP_QB(i, 0, BS_PREP_QA(i, blockIdx.x, 0));
       for (int j = 1; j < nkv; ++j) BS_PREP_K(j, 0);
     }
-    FRSA_STAMP(24);
     for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
       const int nbh = bh + gridDim.x;
       const bool has_next = nbh < prm.BH;
@@ -428,7 +416,6 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       auto drain_kv = [&](int j) {
         mbar_wait(&sm.acc_full[j], hl & 1, abort_flag);
         tc_fence_after();
-        if (hl == 0) FRSA_STAMP(16 + 3 * j);
         float v0[32], v1[32];
         tmem_ld32(tDV + lane_off, v0);
         tmem_ld32(tDV + lane_off + 32, v1);
@@ -449,48 +436,52 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           tma_store_wait_read();
           mbar_arrive(&sm.kv_empty[j]);
         }
-        if (hl == 0) FRSA_STAMP(17 + 3 * j);
       };
-      // dQ_i = R^T dQ^_i scale, staged in the (finished) Q_i tile.
+      // dQ_i = R^T dQ^_i scale, staged in the (finished) query slot.
       auto drain_q = [&](int i) {
+        const int sl = qslot(hl * nqt + i);
         mbar_wait(&sm.dq_full[i], hl & 1, abort_flag);
         tc_fence_after();
-        if (hl == 0) FRSA_STAMP(21 + i);
         float v0[32], v1[32];
         tmem_ld32(tDQ + 64 * i + lane_off, v0);
         tmem_ld32(tDQ + 64 * i + lane_off + 32, v1);
         tmem_wait_ld();
-        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[i]), r, smem_u32(sm.q[i]));
+        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[i]), r, smem_u32(sm.q[sl]));
         tc_fence_before();
         fence_proxy_async_smem();
         named_bar(2, 128);
         if (leader) {
           mbar_arrive(&sm.dq_free[i]);
-          tma_store_3d(&tm_dq, sm.q[i], 0, i * kTile, bh);
+          tma_store_3d(&tm_dq, sm.q[sl], 0, i * kTile, bh);
           tma_store_commit();
           tma_store_wait_read();
-          mbar_arrive(&sm.q_empty[i]);
+          mbar_arrive(&sm.q_empty[sl]);
         }
       };
-      // Order: the next head's first key and query tiles are prepared as soon
-      // as their buffers are released, while this head's remaining MMAs run.
+      // Order: each step of the next head is prepared as soon as its buffer
+      // is free (the next head's first query tile goes to the third slot,
+      // free since the previous head ended), while this head's MMAs run.
+      QPrep a0{0.f, 0.f}, a1{0.f, 0.f};
       drain_kv(0);
-      if (has_next) BS_PREP_K(0, hl + 1);
-      drain_q(0);
-      if (has_next) BS_PREP_Q(0, nbh, hl + 1);
-      if (hl == 0) FRSA_STAMP(18);
-      for (int t = 1; t < nkv; ++t) {
-        drain_q(t);
-        drain_kv(t);
-      }
       if (has_next) {
-        for (int i = 1; i < nqt; ++i) BS_PREP_Q(i, nbh, hl + 1);
-        for (int j = 1; j < nkv; ++j) BS_PREP_K(j, hl + 1);
+        a0 = BS_PREP_QA(0, nbh, hl + 1);
+        BS_PREP_K(0, hl + 1);
       }
-      if (hl == 0) FRSA_STAMP(23);
+      drain_q(0);
+      if (has_next) {
+        BS_PREP_QB(0, hl + 1, a0);
+        if (nqt > 1) a1 = BS_PREP_QA(1, nbh, hl + 1);
+      }
+      if (nkv > 1) {
+        drain_q(1);
+        if (has_next) BS_PREP_QB(1, hl + 1, a1);
+        drain_kv(1);
+        if (has_next) BS_PREP_K(1, hl + 1);
+      }
     }
 #undef BS_PREP_K
-#undef BS_PREP_Q
+#undef BS_PREP_QA
+#undef BS_PREP_QB
   }
 
   tc_fence_before();

@@ -50,8 +50,8 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 // ---------------------------------------------------------------- tracing
 // Trace builds (-DFRSA_TRACE) record %globaltimer at phase boundaries of the
-// first 4096 CTAs, from thread FRSA_STAMP_TID (the first compute thread), into
-// g_trace[cta * 32 + slot]; frsa_trace_copy reads them back. Normal builds
+// first 2048 CTAs, from thread FRSA_STAMP_TID (the first compute thread), into
+// g_trace[cta * 64 + slot]; frsa_trace_copy reads them back. Normal builds
 // compile the stamps away.
 #ifndef FRSA_STAMP_TID
 #define FRSA_STAMP_TID 64
@@ -188,6 +188,14 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int 
   asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// Prefetch [p, p + bytes) into L2 (rounded out to 16-byte boundaries).
+__device__ __forceinline__ void prefetch_l2_bytes(const void* p, uint32_t bytes) {
+  const uint64_t a = reinterpret_cast<uint64_t>(p);
+  const uint64_t lo = a & ~uint64_t(15), hi = (a + bytes + 15) & ~uint64_t(15);
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"(static_cast<uint32_t>(hi - lo))
                : "memory");
 }
 
