@@ -16,17 +16,21 @@
 // tensor core) and frees the P tile, whose space holds a third query-tile
 // slot: the next head's query tiles load and are prepared a head ahead.
 //
-// Warp roles (16 warps, 512 threads):
+// Warp roles (20 warps, 640 threads):
 //   warp 0        TMA producer (K, V, Q, dO tiles; the next head's tiles, O and
 //                 lse into L2)
 //   warp 1        TMEM allocator + MMA issuer
 //   warps 2..3    idle (complete warpgroup 0 for the register rebalancing)
 //   warps 4..11   two elementwise warpgroups: warpgroup g computes P and dS for
 //                 query columns [64 g, 64 g + 64) of each iteration
-//   warps 12..15  aux warpgroup: operand preparation (RoPE of K and Q in shared
-//                 memory, lse2 and Delta = rowsum(dO O)) and the epilogues
-//                 (dV, dK = R^T dK^ scale, dQ = R^T dQ^ scale: TMEM rows staged
-//                 in the finished K/V/Q tiles and written by TMA stores)
+//   warps 12..15  rotation warpgroup: RoPE of the K and Q tiles in shared
+//                 memory, lse2, and the dQ = R^T dQ^ scale epilogue
+//   warps 16..19  Delta warpgroup: Delta = rowsum(dO O) and the dV and
+//                 dK = R^T dK^ scale epilogues
+//   (epilogues: TMEM rows staged in the finished K/V/Q tiles, written by TMA
+//   stores; thread = tile row = TMEM lane). The two groups split the per-head
+//   preparation and epilogue work, which is latency-bound, so that it keeps up
+//   with the tensor core and the elementwise warps.
 //
 // TMEM columns: [0,128) S^T (P packed: columns [64 g, 64 g + 32) hold query
 // columns [64 g, 64 g + 64)), [128,256) dP^T (dS packed likewise), [256,320)
@@ -35,9 +39,9 @@
 // Query tiles rotate through three shared slots: fill u = hl * nqt + i of this
 // CTA (head hl, tile i) uses slot u % 3, and its barriers' phase is (u / 3) & 1.
 //
-// Registers: launched at 128 per thread (512 x 128 = 65536), then warpgroup 0
-// drops to 64, the aux warpgroup rises to 192 and the elementwise warpgroups
-// keep 128: 128*64 + 128*192 + 256*128 = 65536.
+// Registers: launched at 96 per thread (640 x 96 = 61440), then warpgroup 0
+// drops to 56, the two aux warpgroups to 80 and the elementwise warpgroups
+// rise to 128: 128*56 + 256*80 + 256*128 = 60416 <= 61440.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
@@ -49,9 +53,9 @@ namespace frsa {
 
 namespace {
 
-constexpr int kBsThreads = 512;
+constexpr int kBsThreads = 640;
 constexpr int kQSlots = 3;
-constexpr uint32_t kBsRegsCtl = 64, kBsRegsAux = 192, kBsRegsElem = 128;
+constexpr uint32_t kBsRegsCtl = 56, kBsRegsAux = 80, kBsRegsElem = 128;
 
 struct BsSmem {
   uint8_t k[2][kChunkBytes];
@@ -89,34 +93,27 @@ struct BsParams {
 __device__ __forceinline__ int qslot(int u) { return u % kQSlots; }
 __device__ __forceinline__ uint32_t qphase(int u) { return static_cast<uint32_t>(u / kQSlots) & 1u; }
 
-// Aux-warpgroup steps (thread = tile row r); RoPE tables come from the
-// shared table tiles (identical for every head, filled once).
-template <typename T>
-__device__ __forceinline__ void bs_prep_k(BsSmem& sm, int j, int hl, int r, int D, bool leader,
-                                          volatile int* abort_flag) {
-  mbar_wait(&sm.kv_full[j], hl & 1, abort_flag);
-  rotate_row_t<T>(smem_u32(sm.k[j]), smem_u32(sm.tab[j]), r, D);
+// Aux steps (thread = tile row r).
+
+// Rotation group: publish lse2 of fill u and mark its rotated tile ready.
+// Runs once the elementwise warps are done with fill u - 2 (same entry).
+__device__ __forceinline__ void bs_pub_lse(BsSmem& sm, int u, int r, bool leader, float lse2) {
+  sm.lse2[u & 1][r] = lse2;
   fence_proxy_async_smem();
   named_bar(2, 128);
-  if (leader) mbar_arrive(&sm.k_ready[j]);
+  if (leader) mbar_arrive(&sm.q_ready[qslot(u)]);
 }
 
-// Query-tile preparation, part A: rotate the tile in its slot and compute
-// this row's Delta = rowsum(O dO) (dO from the unrotated shared tile); the
-// row's lse2 and Delta are returned, to be published by part B.
-struct QPrep {
-  float lse2, delta;
-};
-
+// Delta group: Delta = rowsum(O dO) of query tile i (fill u) with dO from the
+// shared tile and O read from global memory (L2, prefetched).
 template <typename T>
-__device__ __forceinline__ QPrep bs_prep_qa(BsSmem& sm, const BsParams& prm, int i, int bh, int hl,
+__device__ __forceinline__ float bs_delta_q(BsSmem& sm, const BsParams& prm, int i, int bh, int hl,
                                             int r, volatile int* abort_flag) {
   const int N = prm.N, D = prm.D;
   const int q0 = i * kTile;
   const int u = hl * prm.nqt + i, sl = qslot(u);
   const size_t row0 = static_cast<size_t>(bh) * N;
   const bool qv = q0 + r < N;
-  const float lsev = qv ? prm.lse[row0 + q0 + r] : 0.f;
   // O row r (8 granules), read before the tile wait so the load overlaps it.
   uint4 og[8];
   const uint4* orow =
@@ -125,7 +122,6 @@ __device__ __forceinline__ QPrep bs_prep_qa(BsSmem& sm, const BsParams& prm, int
   for (int g = 0; g < 8; ++g)
     og[g] = (qv && 8 * g < D) ? __ldg(orow + g) : make_uint4(0u, 0u, 0u, 0u);
   mbar_wait(&sm.q_full[sl], qphase(u), abort_flag);
-  rotate_row_t<T>(smem_u32(sm.q[sl]), smem_u32(sm.tab[i]), r, D);
   const uint32_t dob = smem_u32(sm.dO[sl]);
   float dl = 0.f;
 #pragma unroll
@@ -142,20 +138,28 @@ __device__ __forceinline__ QPrep bs_prep_qa(BsSmem& sm, const BsParams& prm, int
     }
   }
   if (prm.delta_out != nullptr && qv) prm.delta_out[row0 + q0 + r] = dl;
-  // Padded query rows get lse2 = +inf, so their P (and dS) is exactly 0.
-  return QPrep{qv ? lsev * 1.4426950408889634f : INFINITY, dl};
+  return dl;
 }
 
-// Part B: publish lse2 / Delta and mark the tile ready. Runs once the
-// elementwise warps are done with query-tile fill u - 2 (same entry).
-__device__ __forceinline__ void bs_prep_qb(BsSmem& sm, const BsParams& prm, int i, int hl, int r,
-                                           bool leader, QPrep v) {
-  const int u = hl * prm.nqt + i;
-  sm.lse2[u & 1][r] = v.lse2;
-  sm.delta[u & 1][r] = v.delta;
-  fence_proxy_async_smem();
-  named_bar(2, 128);
+// Delta group: publish Delta of fill u (same rule as bs_pub_lse).
+__device__ __forceinline__ void bs_pub_delta(BsSmem& sm, int u, int r, bool leader, float dl) {
+  sm.delta[u & 1][r] = dl;
+  named_bar(3, 128);
   if (leader) mbar_arrive(&sm.q_ready[qslot(u)]);
+}
+
+// TMEM accumulator row [tcol, tcol + 64) of this thread's lane -> scaled
+// (optionally R^T-unrotated) 16-bit row r of a shared tile, in two halves.
+template <typename T>
+__device__ __forceinline__ void bs_stage(uint32_t tcol, float scale, uint32_t tab, int r,
+                                         uint32_t tile) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float v[32];
+    tmem_ld32(tcol + 32 * h, v);
+    tmem_wait_ld();
+    stage_half_t<T>(v, h, scale, tab, r, tile);
+  }
 }
 
 template <typename T>
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     for (int s = 0; s < kQSlots; ++s) {
       mbar_init(&sm.q_full[s], 1);
       mbar_init(&sm.q_empty[s], 1);
-      mbar_init(&sm.q_ready[s], 1);
+      mbar_init(&sm.q_ready[s], 2);   // rotation group (Q^, lse2) + Delta group
     }
     mbar_init(&sm.st_full, 1);
     mbar_init(&sm.ds_full, 1);
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
-  FRSA_STAMP(31);
+  FRSA_STAMP(63);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -269,17 +273,21 @@ __global__ void __launch_bounds__(kBsThreads, 1)
         mbar_wait(&sm.k_ready[j], hl & 1, abort_flag);
         mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);
         tc_fence_after();
+        if (it >= 5 && it < 9) FRSA_STAMP_T(49 + 2 * (it - 5), 32);
+#pragma unroll 1
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
           mma_ss(tST, sw128_desc(smem_u32(sm.k[j]) + koff, 16, 1024),
                  sw128_desc(smem_u32(sm.q[sl]) + koff, 16, 1024), idS, kk > 0);
         }
+#pragma unroll 1
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
           mma_ss(tDPT, sw128_desc(smem_u32(sm.v[j]) + koff, 16, 1024),
                  sw128_desc(smem_u32(sm.dO[sl]) + koff, 16, 1024), idS, kk > 0);
         }
         mma_commit(&sm.st_full);
+        if (it >= 4 && it < 12) FRSA_STAMP_T(16 + it - 4, 32);
       };
       auto issue_grads = [&](int it) __attribute__((always_inline)) {
         const int hl = it / per_head, w = it - hl * per_head;
@@ -296,6 +304,8 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           mbar_wait(&sm.dq_free[i], (hl - 1) & 1, abort_flag);  // previous head's dQ_i drained
           tc_fence_after();
         }
+        if (it >= 4 && it < 12) FRSA_STAMP_T(24 + it - 4, 32);
+#pragma unroll 1
         for (int kk = 0; kk < kTile / 16; ++kk) {
           // Query columns [16 kk, 16 kk + 16) of P / dS: packed TMEM columns
           // 64 (kk / 4) + 8 (kk % 4).
@@ -309,11 +319,13 @@ __global__ void __launch_bounds__(kBsThreads, 1)
                  idKV, acc);
         }
         // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
+#pragma unroll 1
         for (int kk = 0; kk < kTile / 16; ++kk) {
           const uint32_t acc = (j == 0 && kk == 0) ? 0u : 1u;
           mma_ss(tmem + 384 + 64 * i, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
                  sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
         }
+        if (it >= 4 && it < 8) FRSA_STAMP_T(48 + 2 * (it - 4), 32);
         // K_j/V_j and the query slot are released by the aux warpgroup once it
         // has staged the finished gradients in them and their stores have read them.
         if (i == nqt - 1) mma_commit(&sm.acc_full[j]);
@@ -323,10 +335,10 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       // so they follow its gradient products in the (in-order) MMA pipe; their
       // completion (st_full) also tells the elementwise warps that the dQ
       // product has read the shared dS tile.
-      if (total > 0) issue_st(0);
-      for (int it = 0; it < total; ++it) {
-        issue_grads(it);
-        if (it + 1 < total) issue_st(it + 1);
+      // (One call site each keeps this warp's code small.)
+      for (int it = 0; it <= total; ++it) {
+        if (it > 0) issue_grads(it - 1);
+        if (it < total) issue_st(it);
       }
     }
   } else if (warp < 12) {
@@ -347,6 +359,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);   // lse2 / Delta of this query tile
       mbar_wait(&sm.st_full, it & 1, abort_flag);
       tc_fence_after();
+      if (it >= 4 && it < 12) FRSA_STAMP_T(2 * (it - 4), 128);
       const uint32_t lbase = smem_u32(&sm.lse2[u & 1][g * 64]);
       const uint32_t ebase = smem_u32(&sm.delta[u & 1][g * 64]);
 #pragma unroll
@@ -383,105 +396,131 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       tc_fence_before();
       named_bar(1, 256);
       if (leader) mbar_arrive(&sm.ds_full);
+      if (it >= 4 && it < 12) FRSA_STAMP_T(2 * (it - 4) + 1, 128);
     }
   } else {
-    setmaxnreg_inc<kBsRegsAux>();
-    // ------------------------------------------------------------ aux warpgroup
-    // Thread = tile row = TMEM lane (r).
-    const int aw = warp - 12;            // 0..3 == TMEM lane quarter
+    setmaxnreg_dec<kBsRegsAux>();
+    // ------------------------------------------------------------ aux warpgroups
+    const bool rot = warp < 16;          // rotation group (else Delta group)
+    const int aw = warp & 3;             // TMEM lane quarter
     const int r = aw * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(aw * 32) << 16;
-    const bool leader = threadIdx.x == 384;
-    // Table tiles: row r of token tiles 0 and 1 (pos < 0 rows are identity).
-    store_tabrow(smem_u32(sm.tab[0]), r, rope_pos(r, N, prm.has_cls), D, prm.cosp, prm.sinp);
-    store_tabrow(smem_u32(sm.tab[1]), r, rope_pos(kTile + r, N, prm.has_cls), D, prm.cosp,
-                 prm.sinp);
-    named_bar(2, 128);
-#define BS_PREP_K(j, hl) bs_prep_k<T>(sm, j, hl, r, D, leader, abort_flag)
-#define BS_PREP_QA(i, bh, hl) bs_prep_qa<T>(sm, prm, i, bh, hl, r, abort_flag)
-#define BS_PREP_QB(i, hl, v) bs_prep_qb(sm, prm, i, hl, r, leader, v)
+    const bool leader = threadIdx.x == (rot ? 384 : 512);
+    // Table tiles: row r of token tiles 0 (rotation group) and 1 (Delta
+    // group); pos < 0 rows are identity.
+    store_tabrow(smem_u32(sm.tab[rot ? 0 : 1]), r, rope_pos((rot ? 0 : kTile) + r, N, prm.has_cls),
+                 D, prm.cosp, prm.sinp);
+    named_bar(4, 256);
     const uint32_t tDQ = tmem + 384;
-    int hl = 0;
-    if ((int)blockIdx.x < prm.BH) {
-      BS_PREP_K(0, 0);
-      for (int i = 0; i < nqt; ++i) BS_PREP_QB(i, 0, BS_PREP_QA(i, blockIdx.x, 0));
-      for (int j = 1; j < nkv; ++j) BS_PREP_K(j, 0);
-    }
-    for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
-      const int nbh = bh + gridDim.x;
-      const bool has_next = nbh < prm.BH;
-      // dV_j, dK_j = R^T dK^_j scale: TMEM rows -> 16-bit rows staged in the
-      // (finished) V_j and K_j tiles -> TMA stores; K_j/V_j are released once
-      // the stores have read them.
-      auto drain_kv = [&](int j) {
-        mbar_wait(&sm.acc_full[j], hl & 1, abort_flag);
-        tc_fence_after();
-        float v0[32], v1[32];
-        tmem_ld32(tDV + lane_off, v0);
-        tmem_ld32(tDV + lane_off + 32, v1);
-        tmem_wait_ld();
-        stage_row_t<T>(v0, v1, 1.f, 0u, r, smem_u32(sm.v[j]));
-        tmem_ld32(tDK + lane_off, v0);
-        tmem_ld32(tDK + lane_off + 32, v1);
-        tmem_wait_ld();
-        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[j]), r, smem_u32(sm.k[j]));
-        tc_fence_before();
-        fence_proxy_async_smem();
-        named_bar(2, 128);
-        if (leader) {
-          mbar_arrive(&sm.acc_free);
-          tma_store_3d(&tm_dv, sm.v[j], 0, j * kTile, bh);
-          tma_store_3d(&tm_dk, sm.k[j], 0, j * kTile, bh);
-          tma_store_commit();
-          tma_store_wait_read();
-          mbar_arrive(&sm.kv_empty[j]);
+    // Each group runs its steps from a schedule through one loop, so that
+    // every step's code appears once: this work runs a few times per head
+    // between long waits, and a large body would fall out of the instruction
+    // cache each time.
+    //
+    // Schedules: entry k of a list is 4 bits at bit 4k: bits 0-1 step type,
+    // bit 2 tile index, bit 3 "for the next head". The first head gets a
+    // prelude list; every head then runs its list (entries marked "next" are
+    // skipped for the CTA's last head).
+    //   rotation group, types: 0 rotate query tile, 1 rotate key tile,
+    //     2 dQ epilogue, 3 publish lse2 (query tile ready);
+    //     head list  R0n K0n D0 P0n R1n D1 P1n K1n  (nqt = 1: the first 4)
+    //     prelude    nqt 2: R0 P0 R1 P1 K0 K1;  nqt 1: R0 P0 K0
+    //   Delta group, types: 0 dV/dK epilogue, 1 Delta of a query tile,
+    //     2 wait until this head's query tile is done, then publish Delta,
+    //     3 publish Delta;
+    //     head list  V0 E0n W0n E1n W1n V1  (nqt = 1: the first 3)
+    //     prelude    E0 P0 E1 P1  (nqt = 1: the first 2)
+    const uint32_t head_list = rot ? 0xdf6cb298u : 0x4eda90u;
+    const uint32_t pre_list = rot ? (nqt > 1 ? 0x517430u : 0x130u) : 0x7531u;
+    const int head_len = rot ? 4 * nqt : 3 * nqt;
+    const int pre_len = rot ? 2 * nqt + nkv : 2 * nqt;
+    float held0 = 0.f, held1 = 0.f;   // lse2 (rotation) / Delta of the tiles in flight
+    int hl = 0, bh = blockIdx.x, step = 0;
+    bool prelude = true;
+    while (bh < prm.BH) {
+      const uint32_t e = ((prelude ? pre_list : head_list) >> (4 * step)) & 0xFu;
+      const int type = e & 3, idx = (e >> 2) & 1;
+      const bool nxt = (e >> 3) & 1;
+      const int tbh = nxt ? bh + (int)gridDim.x : bh;   // head this step works on
+      const int thl = nxt ? hl + 1 : hl;
+      if (tbh < prm.BH) {
+        const int u = thl * nqt + idx, sl = qslot(u);
+        if (rot) {
+          if (type <= 1) {
+            // Rotate a query (type 0) or key (type 1) tile in place.
+            const bool isq = type == 0;
+            const bool qv = idx * kTile + r < N;
+            const float lsev =
+                (isq && qv) ? prm.lse[static_cast<size_t>(tbh) * N + idx * kTile + r] : 0.f;
+            mbar_wait(isq ? &sm.q_full[sl] : &sm.kv_full[idx], isq ? qphase(u) : (thl & 1),
+                      abort_flag);
+            rotate_row_t<T>(smem_u32(isq ? sm.q[sl] : sm.k[idx]), smem_u32(sm.tab[idx]), r, D);
+            if (isq) {
+              // Padded query rows get lse2 = +inf: their P and dS are exactly 0.
+              const float l2 = qv ? lsev * 1.4426950408889634f : INFINITY;
+              if (idx) held1 = l2; else held0 = l2;
+            } else {
+              fence_proxy_async_smem();
+              named_bar(2, 128);
+              if (leader) mbar_arrive(&sm.k_ready[idx]);
+            }
+          } else if (type == 2) {
+            // dQ_i = R^T dQ^_i scale, staged in the (finished) query slot.
+            mbar_wait(&sm.dq_full[idx], thl & 1, abort_flag);
+            tc_fence_after();
+            bs_stage<T>(tDQ + 64 * idx + lane_off, prm.scale, smem_u32(sm.tab[idx]), r,
+                        smem_u32(sm.q[sl]));
+            tc_fence_before();
+            fence_proxy_async_smem();
+            named_bar(2, 128);
+            if (leader) {
+              mbar_arrive(&sm.dq_free[idx]);
+              tma_store_3d(&tm_dq, sm.q[sl], 0, idx * kTile, tbh);
+              tma_store_commit();
+              tma_store_wait_read();
+              mbar_arrive(&sm.q_empty[sl]);
+            }
+          } else {
+            bs_pub_lse(sm, u, r, leader, idx ? held1 : held0);
+          }
+        } else {
+          if (type == 0) {
+            // dV_j, dK_j = R^T dK^_j scale, staged in the (finished) V_j and K_j tiles.
+            mbar_wait(&sm.acc_full[idx], thl & 1, abort_flag);
+            tc_fence_after();
+            bs_stage<T>(tDV + lane_off, 1.f, 0u, r, smem_u32(sm.v[idx]));
+            bs_stage<T>(tDK + lane_off, prm.scale, smem_u32(sm.tab[idx]), r, smem_u32(sm.k[idx]));
+            tc_fence_before();
+            fence_proxy_async_smem();
+            named_bar(3, 128);
+            if (leader) {
+              mbar_arrive(&sm.acc_free);
+              tma_store_3d(&tm_dv, sm.v[idx], 0, idx * kTile, tbh);
+              tma_store_3d(&tm_dk, sm.k[idx], 0, idx * kTile, tbh);
+              tma_store_commit();
+              tma_store_wait_read();
+              mbar_arrive(&sm.kv_empty[idx]);
+            }
+          } else if (type == 1) {
+            const float dl = bs_delta_q<T>(sm, prm, idx, tbh, thl, r, abort_flag);
+            if (idx) held1 = dl; else held0 = dl;
+          } else {
+            // Entry (u & 1) is free once fill u - 2 (this head's tile idx) is done.
+            if (type == 2) mbar_wait(&sm.dq_full[idx], hl & 1, abort_flag);
+            bs_pub_delta(sm, u, r, leader, idx ? held1 : held0);
+          }
         }
-      };
-      // dQ_i = R^T dQ^_i scale, staged in the (finished) query slot.
-      auto drain_q = [&](int i) {
-        const int sl = qslot(hl * nqt + i);
-        mbar_wait(&sm.dq_full[i], hl & 1, abort_flag);
-        tc_fence_after();
-        float v0[32], v1[32];
-        tmem_ld32(tDQ + 64 * i + lane_off, v0);
-        tmem_ld32(tDQ + 64 * i + lane_off + 32, v1);
-        tmem_wait_ld();
-        stage_row_t<T>(v0, v1, prm.scale, smem_u32(sm.tab[i]), r, smem_u32(sm.q[sl]));
-        tc_fence_before();
-        fence_proxy_async_smem();
-        named_bar(2, 128);
-        if (leader) {
-          mbar_arrive(&sm.dq_free[i]);
-          tma_store_3d(&tm_dq, sm.q[sl], 0, i * kTile, bh);
-          tma_store_commit();
-          tma_store_wait_read();
-          mbar_arrive(&sm.q_empty[sl]);
+      }
+      if (++step == (prelude ? pre_len : head_len)) {
+        step = 0;
+        if (prelude) {
+          prelude = false;
+        } else {
+          bh += gridDim.x;
+          ++hl;
         }
-      };
-      // Order: each step of the next head is prepared as soon as its buffer
-      // is free (the next head's first query tile goes to the third slot,
-      // free since the previous head ended), while this head's MMAs run.
-      QPrep a0{0.f, 0.f}, a1{0.f, 0.f};
-      drain_kv(0);
-      if (has_next) {
-        a0 = BS_PREP_QA(0, nbh, hl + 1);
-        BS_PREP_K(0, hl + 1);
-      }
-      drain_q(0);
-      if (has_next) {
-        BS_PREP_QB(0, hl + 1, a0);
-        if (nqt > 1) a1 = BS_PREP_QA(1, nbh, hl + 1);
-      }
-      if (nkv > 1) {
-        drain_q(1);
-        if (has_next) BS_PREP_QB(1, hl + 1, a1);
-        drain_kv(1);
-        if (has_next) BS_PREP_K(1, hl + 1);
       }
     }
-#undef BS_PREP_K
-#undef BS_PREP_QA
-#undef BS_PREP_QB
   }
 
   tc_fence_before();

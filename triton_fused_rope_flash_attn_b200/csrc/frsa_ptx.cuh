@@ -131,26 +131,44 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and
-// leaves the CTA in abort mode) if the wait timed out or the CTA was already
-// aborting.
+// leaves the CTA in abort mode) if the wait timed out (FRSA_WAIT_LIMIT_NS) or
+// the CTA was already aborting. The loop is one short PTX block so that the
+// many wait sites of a kernel stay small in the instruction cache.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((it & 7u) == 0u) {
-      if (*abort_flag) return false;
-      const uint64_t now = globaltimer();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > FRSA_WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        atomicExch(&g_dev_status, FRSA_DEV_TIMEOUT);
-        return false;
-      }
-    }
+  uint32_t ok;
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p, q;\n\t"
+      ".reg .u64 t0, t1;\n\t"
+      ".reg .u32 ab;\n\t"
+      "mov.u32 %0, 1;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "@p bra WAIT_DONE;\n\t"
+      "mov.u64 t0, %%globaltimer;\n\t"
+      "WAIT_LOOP:\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "@p bra WAIT_DONE;\n\t"
+      "ld.volatile.shared.u32 ab, [%4];\n\t"
+      "setp.ne.u32 q, ab, 0;\n\t"
+      "@q bra WAIT_FAIL;\n\t"
+      "mov.u64 t1, %%globaltimer;\n\t"
+      "sub.u64 t1, t1, t0;\n\t"
+      "setp.lt.u64 q, t1, %5;\n\t"
+      "@q bra WAIT_LOOP;\n\t"
+      "WAIT_FAIL:\n\t"
+      "mov.u32 %0, 0;\n\t"
+      "WAIT_DONE:\n\t"
+      "}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u),
+        "r"(smem_u32(const_cast<int*>(abort_flag))), "l"(static_cast<uint64_t>(FRSA_WAIT_LIMIT_NS))
+      : "memory");
+  if (ok) return true;
+  if (*abort_flag == 0) {   // this wait timed out (not an abort raised elsewhere)
+    *abort_flag = 1;
+    atomicExch(&g_dev_status, FRSA_DEV_TIMEOUT);
   }
+  return false;
 }
 
 // ---------------------------------------------------------------- fences

@@ -324,4 +324,35 @@ __device__ __forceinline__ void stage_row_t(const float (&v0)[32], const float (
   for (int g = 0; g < 8; ++g) sts_u4(tile + sw128_off(r, g), row_granule_t<T>(v0, v1, g, scale, tab, r));
 }
 
+// Half h (columns [32 h, 32 h + 32), granules 4h..4h+3) of such a row, given
+// as its 32 values, scaled, optionally R^T-unrotated, staged in a shared tile.
+template <typename T>
+__device__ __forceinline__ void stage_half_t(const float (&v)[32], int h, float scale,
+                                             uint32_t tab, int r, uint32_t tile) {
+#pragma unroll
+  for (int gl = 0; gl < 4; ++gl) {
+    const int g = 4 * h + gl;
+    uint32_t tw[4] = {0u, 0u, 0u, 0u};
+    if (tab != 0u) {
+      const uint4 t = lds_u4(tab + sw128_off(r, g));
+      tw[0] = t.x; tw[1] = t.y; tw[2] = t.z; tw[3] = t.w;
+    }
+    float u[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float a = v[8 * gl + 2 * e] * scale;
+      float b = v[8 * gl + 2 * e + 1] * scale;
+      if (tab != 0u) {
+        const float2 cs = Elt<__half>::unpack(tw[e]);
+        const float a2 = a * cs.x + b * cs.y;
+        b = b * cs.x - a * cs.y;
+        a = a2;
+      }
+      u[2 * e] = a;
+      u[2 * e + 1] = b;
+    }
+    sts_u4(tile + sw128_off(r, g), pack8<T>(u));
+  }
+}
+
 }  // namespace frsa
