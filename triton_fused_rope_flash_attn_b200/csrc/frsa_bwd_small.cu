@@ -184,6 +184,9 @@ __global__ void __launch_bounds__(kBsThreads, 1)
   const int ksteps = DP >> 4;
   const int nqt = prm.nqt, nkv = prm.nkv;
   volatile int* abort_flag = &sm.abort_flag;
+  // Number of 16-token steps of tile t that hold tokens (8 for a full tile):
+  // the products skip the steps of the last tile that are only padding.
+  auto valid16 = [&](int t) -> int { return min(8, (N - t * kTile + 15) >> 4); };
 
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
@@ -263,7 +266,6 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr bool kBf = Elt<T>::kBf16;
-      const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);   // S^T, dP^T
       const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
       const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
       auto issue_st = [&](int it) __attribute__((always_inline)) {
@@ -274,6 +276,8 @@ __global__ void __launch_bounds__(kBsThreads, 1)
         mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);
         tc_fence_after();
         if (it >= 5 && it < 9) FRSA_STAMP_T(49 + 2 * (it - 5), 32);
+        // S^T, dP^T: only the query columns that hold tokens (rounded up to 16).
+        const uint32_t idS = idesc_f16(kBf, 128, 16 * valid16(i), false, false);
 #pragma unroll 1
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
@@ -305,8 +309,9 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           tc_fence_after();
         }
         if (it >= 4 && it < 12) FRSA_STAMP_T(24 + it - 4, 32);
+        const int kq = valid16(i), kkeys = valid16(j);
 #pragma unroll 1
-        for (int kk = 0; kk < kTile / 16; ++kk) {
+        for (int kk = 0; kk < kq; ++kk) {
           // Query columns [16 kk, 16 kk + 16) of P / dS: packed TMEM columns
           // 64 (kk / 4) + 8 (kk % 4).
           const uint32_t pcol = 64 * (kk >> 2) + 8 * (kk & 3);
@@ -318,9 +323,11 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           mma_ts(tDK, tDPT + pcol, sw128_desc(smem_u32(sm.q[sl]) + kk * 2048, kChunkBytes, 1024),
                  idKV, acc);
         }
-        // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
+        // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d]
+        // MN-major. Query rows past the computed columns read stale dS; they
+        // only reach dQ rows past N, which are never stored.
 #pragma unroll 1
-        for (int kk = 0; kk < kTile / 16; ++kk) {
+        for (int kk = 0; kk < kkeys; ++kk) {
           const uint32_t acc = (j == 0 && kk == 0) ? 0u : 1u;
           mma_ss(tmem + 384 + 64 * i, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
                  sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
@@ -362,8 +369,10 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       if (it >= 4 && it < 12) FRSA_STAMP_T(2 * (it - 4), 128);
       const uint32_t lbase = smem_u32(&sm.lse2[u & 1][g * 64]);
       const uint32_t ebase = smem_u32(&sm.delta[u & 1][g * 64]);
+      const int ncol = 16 * valid16(i);   // query columns the MMAs computed
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
+        if (64 * g + 32 * hh >= ncol) continue;   // padding only: never read
         float sv[32], dp[32];
         tmem_ld32(tST + lane_off + g * 64 + hh * 32, sv);
         tmem_ld32(tDPT + lane_off + g * 64 + hh * 32, dp);
