@@ -305,7 +305,9 @@ def gpu_arm(args, world, rank, local):
         ach = fb / (bwd_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4)}
-    roof.update({"traffic": load_traffic(args.config), "kernel": "bwd_kernel",
+    small = N <= 256 and D <= 64
+    traffic = load_traffic(args.config) if not args.batch else None
+    roof.update({"traffic": traffic, "kernel": "bwd_small_kernel" if small else "bwd_kernel",
                  "peak_source": psrc, "algorithmic_bytes_per_launch": bb,
                  "algorithmic_flops_per_launch": fb,
                  "tensor_frac": round(fb / (bwd_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)})
