@@ -14,6 +14,7 @@ from .attention import (  # noqa: F401
     fused_rope_attention_fwd,
     fused_rope_attention_bwd,
 )
+from .ops import sdpa_fa_rope_op  # noqa: F401  (registers torch.ops.frsa.*)
 
 __all__ = [
     "build_axial_rope_pairs",
@@ -23,4 +24,5 @@ __all__ = [
     "sdpa_triton_fa_rope",
     "fused_rope_attention_fwd",
     "fused_rope_attention_bwd",
+    "sdpa_fa_rope_op",
 ]
