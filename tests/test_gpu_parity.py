@@ -146,3 +146,34 @@ def test_delta_rowsum(side, has_cls):
     fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls, delta_out=delta)
     ref = (o.double() * do.double()).sum(-1)
     assert torch.allclose(delta.double(), ref, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("side,has_cls,D,qamp,vamp", [(14, True, 64, 1.0, 1.0),
+                                                      (5, False, 64, 1.0, 1000.0),
+                                                      (7, True, 80, 2.0, 1e-3),
+                                                      (17, True, 64, 1.0, 1.0)])
+def test_fp32_compute_against_oracle(side, has_cls, D, qamp, vamp):
+    """float32 inputs without autocast (the reference's TF32 mode): f16 operands
+    (TF32's 10-bit mantissa) with power-of-two range scaling, fp32 outputs.
+    Checked against the float64 oracle on the same fp32 inputs, relative to the
+    outputs' scale. V and dO are scaled by `vamp` (1000x and 1e-3x: outside or at
+    the edge of f16's range without the scaling); q by `qamp` (sharper softmax)."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, sdpa_triton_fa_rope
+    B, H = 2, 2
+    N = side * side + (1 if has_cls else 0)
+    q, k, v, do = seeded_inputs(B, H, N, D, 1.0, 11)
+    q, v, do = q * qamp, v * vamp, do * vamp
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    qd, kd, vd = (t.cuda().float().requires_grad_(True) for t in (q, k, v))
+    o = sdpa_triton_fa_rope(qd, kd, vd, cs, has_cls=has_cls, H_img=side)
+    o.backward(do.cuda().float())
+    assert o.dtype == torch.float32 and qd.grad.dtype == torch.float32
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    qn, kn, vn, don = (t.double().numpy() for t in (q, k, v, do))
+    o_ref, _ = attn_fwd_np(qn, kn, vn, cos, sin, has_cls)
+    dq_ref, dk_ref, dv_ref = attn_bwd_np(qn, kn, vn, don, cos, sin, has_cls)
+    for name, got, ref in (("o", o, o_ref), ("dq", qd.grad, dq_ref), ("dk", kd.grad, dk_ref),
+                           ("dv", vd.grad, dv_ref)):
+        g = got.detach().double().cpu().numpy()
+        err = np.abs(g - ref).max() / max(np.abs(ref).max(), 1e-30)
+        assert err < 5e-3, (name, err)

@@ -36,7 +36,7 @@ def _ptr(t):
 
 
 def _make_args(q, k, v, cosp, sinp, has_cls, comp, o=None, lse=None, d_o=None, dq=None, dk=None,
-               dv=None, delta=None, workspace=None):
+               dv=None, delta=None, workspace=None, scale=None):
     B, H, N, D = q.shape
     a = _lib.FrsaAttnArgs()
     a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
@@ -50,7 +50,7 @@ def _make_args(q, k, v, cosp, sinp, has_cls, comp, o=None, lse=None, d_o=None, d
     a.has_cls = int(bool(has_cls))
     a.io_dtype = _DT_CODE[comp]
     a.compute_dtype = _DT_CODE[comp]
-    a.scale = 1.0 / math.sqrt(D)
+    a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
     return a
 
 
@@ -71,10 +71,11 @@ def _check_tables(cosp, sinp, N, D, has_cls, device):
         raise ValueError("RoPE tables must be on the same device as Q")
 
 
-def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True):
+def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True, scale=None):
     """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]`` bf16/f16.
 
     Returns ``(o, lse)`` with ``lse`` float32 ``[B, H, N]`` (natural log).
+    ``scale`` multiplies the logits (default ``1/sqrt(D)``).
     """
     comp = q.dtype
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
@@ -82,13 +83,13 @@ def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True):
     B, H, N, D = q.shape
     o = torch.empty_like(q)
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse)
+    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, scale=scale)
     _lib.check(_lib.load().frsa_fwd(a, _stream_handle(q.device)), "frsa_fwd")
     return o, lse
 
 
 def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = True,
-                             delta_out=None):
+                             delta_out=None, scale=None):
     """Backward through the C ABI. Returns ``(dq, dk, dv)`` in ``q.dtype``.
 
     ``delta_out`` (optional float32 ``[B, H, N]``) receives ``rowsum(dO * O)``.
@@ -99,7 +100,7 @@ def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = T
     B, H, N, D = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, d_o=d_o, dq=dq, dk=dk,
-                   dv=dv, delta=delta_out)
+                   dv=dv, delta=delta_out, scale=scale)
     lib = _lib.load()
     ws_bytes = lib.frsa_bwd_workspace_bytes(a)
     ws = None
@@ -108,6 +109,47 @@ def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = T
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws_bytes
     _lib.check(lib.frsa_bwd(a, _stream_handle(q.device)), "frsa_bwd")
+    return dq, dk, dv
+
+
+def _pow2_normaliser(x: torch.Tensor, target: float = 1.0) -> float:
+    """Power of two s with max|x * s| <= target (1 for an all-zero tensor)."""
+    m = float(x.detach().abs().max()) if x.numel() else 0.0
+    if not math.isfinite(m):
+        raise FloatingPointError("non-finite input to the fused attention")
+    if m == 0.0:
+        return 1.0
+    return 2.0 ** math.floor(math.log2(target / m))
+
+
+# float32 compute. The reference computes fp32 inputs with Triton's TF32 dot
+# products (10-bit mantissa operands, fp32 accumulation; fa_rope_full .py:65-73
+# selects float32 as the kernel dtype). Here the operands of every product are
+# held in f16, which has the same 10-bit mantissa, and accumulation stays fp32.
+# f16's narrower exponent range is handled exactly: each input is multiplied
+# by a power of two that brings its largest magnitude to 1 (dO to 1/8, leaving
+# headroom for dV = P^T dO and dQ = dS K), the logit scale absorbs the Q and K
+# factors, and the outputs are divided back. Outputs are returned in float32.
+def _fp32_forward(Q, K, V, COSP, SINP, has_cls):
+    D = Q.shape[-1]
+    sq, sk, sv = _pow2_normaliser(Q), _pow2_normaliser(K), _pow2_normaliser(V)
+    qh, kh, vh = (Q * sq).half(), (K * sk).half(), (V * sv).half()
+    scale = 1.0 / math.sqrt(D) / (sq * sk)
+    oh, lse = fused_rope_attention_fwd(qh, kh, vh, COSP, SINP, has_cls, scale=scale)
+    return oh, lse, (qh, kh, vh, sq, sk, sv, scale)
+
+
+def _fp32_backward(state, oh, lse, dO, COSP, SINP, has_cls):
+    qh, kh, vh, sq, sk, sv, scale = state
+    sd = _pow2_normaliser(dO, 0.125)
+    dq, dk, dv = fused_rope_attention_bwd(qh, kh, vh, oh, lse, (dO * sd).half(), COSP, SINP,
+                                          has_cls, scale=scale)
+    dq = dq.float() * (sq / (sd * sv))
+    dk = dk.float() * (sk / (sd * sv))
+    dv = dv.float() / sd
+    for g in (dq, dk, dv):
+        if not torch.isfinite(g).all():
+            raise FloatingPointError("float32 attention gradient left the f16 operand range")
     return dq, dk, dv
 
 
@@ -128,25 +170,31 @@ class TritonAttention(torch.autograd.Function):
         comp = _sdpa_comp_dtype(Q)
         if not Q.is_cuda:
             raise RuntimeError("sdpa_triton_fa_rope needs CUDA tensors (there is no CPU path)")
-        if comp == torch.float32:
-            raise NotImplementedError(
-                "float32 compute (TF32 tensor cores) is not implemented; run under "
-                "torch.autocast('cuda', dtype=torch.bfloat16) or pass bf16/fp16 tensors")
         COSP, SINP = cos_sin.tables()
         _check_tables(COSP, SINP, SEQ_LEN, HEAD_DIM, has_cls, Q.device)
-        qc, kc, vc = (t.to(comp) for t in (Q, K, V))
-        o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls)
         ctx.comp = comp
         ctx.has_cls = has_cls
         ctx.io_dtypes = (Q.dtype, K.dtype, V.dtype)
+        if comp == torch.float32:
+            Qf, Kf, Vf = (t.float() for t in (Q, K, V))
+            oh, lse, state = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls)
+            ctx.fp32_state = state[3:]
+            ctx.save_for_backward(state[0], state[1], state[2], oh, lse, COSP, SINP)
+            return (oh.float() / state[5]).to(Q.dtype)
+        qc, kc, vc = (t.to(comp) for t in (Q, K, V))
+        o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls)
         ctx.save_for_backward(qc, kc, vc, o, lse, COSP, SINP)
         return o.to(Q.dtype)
 
     @staticmethod
     def backward(ctx, dO):
         qc, kc, vc, o, lse, COSP, SINP = ctx.saved_tensors
-        dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
-                                              ctx.has_cls)
+        if ctx.comp == torch.float32:
+            dq, dk, dv = _fp32_backward((qc, kc, vc) + ctx.fp32_state, o, lse, dO.float(), COSP,
+                                        SINP, ctx.has_cls)
+        else:
+            dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
+                                                  ctx.has_cls)
         qd, kd, vd = ctx.io_dtypes
         return dq.to(qd), dk.to(kd), dv.to(vd), None, None, None
 

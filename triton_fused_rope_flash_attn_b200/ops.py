@@ -19,13 +19,14 @@ dtype).
 """
 from __future__ import annotations
 
+import math
 from typing import Tuple
 
 import torch
 from torch import Tensor
 
-from .attention import (_check_tables, _sdpa_comp_dtype, fused_rope_attention_bwd,
-                        fused_rope_attention_fwd)
+from .attention import (TritonAttention, _check_tables, _sdpa_comp_dtype,
+                        fused_rope_attention_bwd, fused_rope_attention_fwd)
 
 
 @torch.library.custom_op("frsa::attn_fwd", mutates_args=())
@@ -83,9 +84,11 @@ def sdpa_fa_rope_op(Q: Tensor, K: Tensor, V: Tensor, cos_sin, *, has_cls: bool =
     assert (D % 4) == 0, "HEAD_DIM must be divisible by 4 (2D RoPE requires pairs)."
     comp = _sdpa_comp_dtype(Q)
     if comp == torch.float32:
-        raise NotImplementedError(
-            "float32 compute (TF32 tensor cores) is not implemented; run under "
-            "torch.autocast('cuda', dtype=torch.bfloat16) or pass bf16/fp16 tensors")
+        # float32 compute picks per-call power-of-two range factors from the
+        # data, which a traced graph cannot hold: it runs through the
+        # autograd.Function path (eager).
+        return TritonAttention.apply(Q, K, V, cos_sin, math.isqrt(cos_sin.tables()[0].shape[0]),
+                                     has_cls)
     COSP, SINP = cos_sin.tables()
     _check_tables(COSP, SINP, Q.shape[-2], D, has_cls, Q.device)
     q, k, v = (t.to(comp).contiguous() for t in (Q, K, V))
