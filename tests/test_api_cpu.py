@@ -100,11 +100,21 @@ def _args(**kw):
     (dict(has_cls=2), 2),
     (dict(B=0), 2),
     (dict(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_BF16), 4),
-    (dict(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32), 4),
+    (dict(io_dtype=_lib.FRSA_DTYPE_F16, compute_dtype=_lib.FRSA_DTYPE_F32), 4),
+    # float32 in and out (TF32 compute) is a valid forward: it gets as far as
+    # the device check on a machine without an sm_100 GPU.
+    (dict(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32), 8),
     (dict(k=0x1008), 5),
 ])
 def test_fwd_validation_before_device(lib, kw, code):
     assert lib.frsa_fwd(ctypes.byref(_args(**kw)), None) == code
+
+
+def test_bwd_float32_is_forward_only(lib):
+    a = _args(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32)
+    a.d_o = a.dq = a.dk = a.dv = 0x3000
+    assert lib.frsa_bwd(ctypes.byref(a), None) == 4
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(a)) == 0
 
 
 def test_bwd_requires_gradients_and_workspace(lib):

@@ -153,10 +153,13 @@ def test_delta_rowsum(side, has_cls):
                                                       (7, True, 80, 2.0, 1e-3),
                                                       (17, True, 64, 1.0, 1.0)])
 def test_fp32_compute_against_oracle(side, has_cls, D, qamp, vamp):
-    """float32 inputs without autocast (the reference's TF32 mode): f16 operands
-    (TF32's 10-bit mantissa) with power-of-two range scaling, fp32 outputs.
-    Checked against the float64 oracle on the same fp32 inputs, relative to the
-    outputs' scale. V and dO are scaled by `vamp` (1000x and 1e-3x: outside or at
+    """float32 inputs without autocast (the reference's TF32 mode): native TF32
+    forward; backward on f16 operands (TF32's 10-bit mantissa) with power-of-two
+    range scaling; fp32 outputs. Checked against the float64 oracle on the same
+    fp32 inputs, relative to each output's scale, at 1e-2: both halves round
+    every product operand to 10 mantissa bits (TF32 itself does), and the
+    backward recomputes the logits from differently rounded operands than the
+    forward's LSE. V and dO are scaled by `vamp` (1000x and 1e-3x: outside or at
     the edge of f16's range without the scaling); q by `qamp` (sharper softmax)."""
     from triton_fused_rope_flash_attn_b200 import CosSinTable, sdpa_triton_fa_rope
     B, H = 2, 2
@@ -176,4 +179,30 @@ def test_fp32_compute_against_oracle(side, has_cls, D, qamp, vamp):
                            ("dv", vd.grad, dv_ref)):
         g = got.detach().double().cpu().numpy()
         err = np.abs(g - ref).max() / max(np.abs(ref).max(), 1e-30)
-        assert err < 5e-3, (name, err)
+        assert err < 1e-2, (name, err)
+
+
+@pytest.mark.parametrize("side,has_cls,D", [(14, True, 64), (3, False, 64), (16, True, 64),
+                                            (7, True, 80), (5, False, 128), (6, True, 32)])
+def test_tf32_forward_against_oracle(side, has_cls, D):
+    """Native float32 forward (tcgen05 kind::tf32) through the C ABI. TF32 keeps
+    10 mantissa bits of each operand, so the bar is relative: 5e-3 of the
+    output scale (O); LSE within 1e-2 absolute."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, fused_rope_attention_fwd
+    B, H = 2, 3
+    N = side * side + (1 if has_cls else 0)
+    q, k, v, _ = seeded_inputs(B, H, N, D, 1.0, 21)
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    o, lse = fused_rope_attention_fwd(q.cuda().float(), k.cuda().float(), v.cuda().float(),
+                                      cs.COSP, cs.SINP, has_cls)
+    torch.cuda.synchronize()
+    from triton_fused_rope_flash_attn_b200 import _lib
+    assert _lib.load().frsa_query_status() == 0
+    assert o.dtype == torch.float32
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    o_ref, lse_ref = attn_fwd_np(q.double().numpy(), k.double().numpy(), v.double().numpy(),
+                                 cos, sin, has_cls)
+    err = np.abs(o.double().cpu().numpy() - o_ref).max() / np.abs(o_ref).max()
+    assert err < 5e-3, err
+    assert np.abs(lse.double().cpu().numpy() - lse_ref).max() < 1e-2
+

@@ -124,26 +124,27 @@ def _pow2_normaliser(x: torch.Tensor, target: float = 1.0) -> float:
 
 # float32 compute. The reference computes fp32 inputs with Triton's TF32 dot
 # products (10-bit mantissa operands, fp32 accumulation; fa_rope_full .py:65-73
-# selects float32 as the kernel dtype). Here the operands of every product are
-# held in f16, which has the same 10-bit mantissa, and accumulation stays fp32.
-# f16's narrower exponent range is handled exactly: each input is multiplied
-# by a power of two that brings its largest magnitude to 1 (dO to 1/8, leaving
-# headroom for dV = P^T dO and dQ = dS K), the logit scale absorbs the Q and K
-# factors, and the outputs are divided back. Outputs are returned in float32.
+# selects float32 as the kernel dtype). The forward here is the native
+# kind::tf32 kernel (fp32 in and out). The backward runs on the f16 kernels,
+# whose operands have the same 10-bit mantissa as TF32, with accumulation in
+# fp32; f16's narrower exponent range is handled exactly: each operand is
+# multiplied by a power of two that brings its largest magnitude to 1 (dO to
+# 1/8, leaving headroom for dV = P^T dO and dQ = dS K), the logit scale absorbs
+# the Q and K factors, and the gradients are divided back and returned in fp32.
 def _fp32_forward(Q, K, V, COSP, SINP, has_cls):
+    return fused_rope_attention_fwd(Q.contiguous(), K.contiguous(), V.contiguous(), COSP, SINP,
+                                    has_cls)
+
+
+def _fp32_backward(Q, K, V, O, lse, dO, COSP, SINP, has_cls):
     D = Q.shape[-1]
     sq, sk, sv = _pow2_normaliser(Q), _pow2_normaliser(K), _pow2_normaliser(V)
-    qh, kh, vh = (Q * sq).half(), (K * sk).half(), (V * sv).half()
-    scale = 1.0 / math.sqrt(D) / (sq * sk)
-    oh, lse = fused_rope_attention_fwd(qh, kh, vh, COSP, SINP, has_cls, scale=scale)
-    return oh, lse, (qh, kh, vh, sq, sk, sv, scale)
-
-
-def _fp32_backward(state, oh, lse, dO, COSP, SINP, has_cls):
-    qh, kh, vh, sq, sk, sv, scale = state
     sd = _pow2_normaliser(dO, 0.125)
-    dq, dk, dv = fused_rope_attention_bwd(qh, kh, vh, oh, lse, (dO * sd).half(), COSP, SINP,
-                                          has_cls, scale=scale)
+    qh, kh, vh = (Q * sq).half(), (K * sk).half(), (V * sv).half()
+    oh, doh = (O * sv).half(), (dO * sd).half()
+    scale = 1.0 / math.sqrt(D) / (sq * sk)
+    dq, dk, dv = fused_rope_attention_bwd(qh, kh, vh, oh, lse, doh, COSP, SINP, has_cls,
+                                          scale=scale)
     dq = dq.float() * (sq / (sd * sv))
     dk = dk.float() * (sk / (sd * sv))
     dv = dv.float() / sd
@@ -176,11 +177,10 @@ class TritonAttention(torch.autograd.Function):
         ctx.has_cls = has_cls
         ctx.io_dtypes = (Q.dtype, K.dtype, V.dtype)
         if comp == torch.float32:
-            Qf, Kf, Vf = (t.float() for t in (Q, K, V))
-            oh, lse, state = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls)
-            ctx.fp32_state = state[3:]
-            ctx.save_for_backward(state[0], state[1], state[2], oh, lse, COSP, SINP)
-            return (oh.float() / state[5]).to(Q.dtype)
+            Qf, Kf, Vf = (t.float().contiguous() for t in (Q, K, V))
+            o, lse = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls)
+            ctx.save_for_backward(Qf, Kf, Vf, o, lse, COSP, SINP)
+            return o.to(Q.dtype)
         qc, kc, vc = (t.to(comp) for t in (Q, K, V))
         o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls)
         ctx.save_for_backward(qc, kc, vc, o, lse, COSP, SINP)
@@ -190,8 +190,7 @@ class TritonAttention(torch.autograd.Function):
     def backward(ctx, dO):
         qc, kc, vc, o, lse, COSP, SINP = ctx.saved_tensors
         if ctx.comp == torch.float32:
-            dq, dk, dv = _fp32_backward((qc, kc, vc) + ctx.fp32_state, o, lse, dO.float(), COSP,
-                                        SINP, ctx.has_cls)
+            dq, dk, dv = _fp32_backward(qc, kc, vc, o, lse, dO.float(), COSP, SINP, ctx.has_cls)
         else:
             dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
                                                   ctx.has_cls)

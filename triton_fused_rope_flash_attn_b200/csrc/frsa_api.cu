@@ -16,6 +16,7 @@
 #include "frsa_bwd_small.cu"
 #include "frsa_fwd.cu"
 #include "frsa_fwd_small.cu"
+#include "frsa_tf32.cu"
 
 namespace {
 
@@ -57,19 +58,28 @@ bool device_is_sm100() {
 thread_local int g_last_encode_result = 0;
 
 // 3-D map over a contiguous [BH, N, D] 16-bit tensor: dims {D, N, BH}, box
-// {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor.
-bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s) {
+// {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor. For float32
+// tensors (s.f32) the box is {32, 128, 1}: 128 bytes per row as well.
+// atom32: for float32 operands read MN-major by kind::tf32 products, the
+// 128-byte swizzle with 32-byte atoms that such operands need.
+bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s,
+                bool atom32 = false) {
   auto fn = get_encode_fn();
   if (!fn) return false;
+  const cuuint64_t elt = s.f32 ? 4 : 2;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(s.D), static_cast<cuuint64_t>(s.N),
                               static_cast<cuuint64_t>(s.BH)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.D) * 2,
-                                 static_cast<cuuint64_t>(s.D) * s.N * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.D) * elt,
+                                 static_cast<cuuint64_t>(s.D) * s.N * elt};
+  const cuuint32_t box[3] = {s.f32 ? 32u : 64u, 128, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = fn(m, s.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+  const CUtensorMapDataType dt = s.f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : s.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(m, dt,
                         3, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
   return r == CUDA_SUCCESS;
@@ -101,7 +111,8 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   const long long nqt = (a->N + kTile - 1) / kTile;
   if (BH * nqt > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
   if (a->io_dtype != a->compute_dtype) return FRSA_ERR_UNSUPPORTED_DTYPE;
-  if (a->compute_dtype != FRSA_DTYPE_BF16 && a->compute_dtype != FRSA_DTYPE_F16)
+  if (a->compute_dtype != FRSA_DTYPE_BF16 && a->compute_dtype != FRSA_DTYPE_F16 &&
+      a->compute_dtype != FRSA_DTYPE_F32)
     return FRSA_ERR_UNSUPPORTED_DTYPE;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) ||
       !aligned16(a->sinp))
@@ -112,6 +123,7 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   s->has_cls = a->has_cls;
   s->scale = a->scale;
   s->bf16 = a->compute_dtype == FRSA_DTYPE_BF16;
+  s->f32 = a->compute_dtype == FRSA_DTYPE_F32;
   return FRSA_OK;
 }
 
@@ -143,6 +155,7 @@ const char* frsa_strerror(int code) {
 size_t frsa_bwd_workspace_bytes(const frsa_attn_args* a) {
   frsa::LaunchShape s;
   if (validate_common(a, &s) != FRSA_OK) return 0;
+  if (s.f32) return 0;   // no float32 backward through this ABI
   if (!frsa::bwd_needs_workspace(s)) return 0;
   return static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
 }
@@ -158,11 +171,14 @@ int frsa_fwd(const frsa_attn_args* a, void* stream) {
   // (e.g. cudaErrorNotReady from an event poll) must not be blamed on our launch.
   (void)cudaGetLastError();
   CUtensorMap tq, tk, tv, to;
-  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
-      !encode_map(&to, a->o, s))
+  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) ||
+      !encode_map(&tv, a->v, s, /*atom32=*/s.f32) || !encode_map(&to, a->o, s))
     return launch_error("frsa_fwd", cudaSuccess);
-  const cudaError_t e = frsa::launch_fwd(s, tq, tk, tv, to, a->cosp, a->sinp, a->o, a->lse,
-                                         static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      s.f32 ? frsa::launch_fwd_tf32(s, tq, tk, tv, a->cosp, a->sinp, static_cast<float*>(a->o),
+                                    a->lse, st)
+            : frsa::launch_fwd(s, tq, tk, tv, to, a->cosp, a->sinp, a->o, a->lse, st);
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_fwd", e);
 }
 
@@ -170,6 +186,7 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
   frsa::LaunchShape s;
   int rc = validate_common(a, &s);
   if (rc != FRSA_OK) return rc;
+  if (s.f32) return FRSA_ERR_UNSUPPORTED_DTYPE;   // float32: forward only
   if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv)
     return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||

@@ -18,7 +18,8 @@ struct LaunchShape {
   int D;         // head dim (multiple of 8, <= 128)
   int has_cls;
   float scale;
-  bool bf16;     // true: bf16, false: f16
+  bool bf16;     // true: bf16, false: f16 (16-bit kernels)
+  bool f32;      // float32 I/O and TF32 compute (the frsa_tf32.cu kernels)
 };
 
 // Forward. tm_q/k/v: 3-D maps {D, N, BH} with box {64, 128, 1}, 128B swizzle.
@@ -26,6 +27,11 @@ struct LaunchShape {
 cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                        const CUtensorMap& tm_v, const CUtensorMap& tm_o, const float* cosp,
                        const float* sinp, void* o, float* lse, cudaStream_t stream);
+
+// float32 compute on TF32 tensor cores. Maps: {D, N, BH} float32, box {32, 128, 1}.
+cudaError_t launch_fwd_tf32(const LaunchShape& s, const CUtensorMap& tm_q,
+                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, const float* cosp,
+                            const float* sinp, float* o, float* lse, cudaStream_t stream);
 
 // Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
 bool fwd_small_applies(const LaunchShape& s);

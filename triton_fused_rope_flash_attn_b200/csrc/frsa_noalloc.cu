@@ -110,6 +110,7 @@ extern "C" int frsa_bwd_noalloc(const frsa_attn_args* a, void* stream) {
   frsa::LaunchShape s;
   int rc = validate_common(a, &s);
   if (rc != FRSA_OK) return rc;
+  if (s.f32) return FRSA_ERR_UNSUPPORTED_DTYPE;   // 16-bit kernels only
   if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv) return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||
       !aligned16(a->dv) || !aligned16(a->lse))
