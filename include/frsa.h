@@ -129,6 +129,31 @@ const char* frsa_last_error_detail(void);
  * FRSA_ERR_LAUNCH on a sticky CUDA error, else FRSA_OK. */
 int frsa_query_status(void);
 
+/* QKV projection with the 2D RoPE applied in its epilogue: for x [B*N, C]
+ * (token rows), the nn.Linear weight w [3C, C] and bias [3C] (fp32),
+ *   q = R(x w[0:C]^T + b[0:C]), k = R(x w[C:2C]^T + b[C:2C]), v = x w[2C:]^T + b[2C:],
+ * each written as [B, H, N, D] (D = C / H) in `dtype`; R rotates token n with
+ * table row n - has_cls and leaves the CLS token as is. Attention over these
+ * q, k then needs no further rotation (use identity tables). Requires
+ * C % 128 == 0 and D % 32 == 0 (else FRSA_ERR_UNSUPPORTED_D).
+ * No counterpart in the reference: it fuses the projection that precedes the
+ * reference's kernel in timm's attention block (reference README:156-159). */
+typedef struct frsa_qkv_args {
+  const void* x;
+  const void* w;
+  const float* bias;
+  const float* cosp;
+  const float* sinp;
+  void* q;
+  void* k;
+  void* v;
+  int64_t B, N, C, H, n_pos;
+  int32_t has_cls;
+  int32_t dtype;      /* enum frsa_dtype: BF16 or F16 */
+} frsa_qkv_args;
+
+int frsa_qkv_rope(const frsa_qkv_args* args, void* stream);
+
 /* FRSA_ABI_VERSION of the loaded library. */
 int frsa_abi_version(void);
 

@@ -51,3 +51,28 @@ def test_block_matches_fp32_reference(dim, heads, side, has_cls):
 
     assert rel(y.detach(), yr.detach()) < 2e-2
     assert rel(x.grad, xr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("dim,heads,side,has_cls", [(768, 12, 14, True), (384, 6, 7, False)])
+def test_fused_qkv_rope_block_matches_unfused(dim, heads, side, has_cls):
+    """RoPE in the QKV-projection epilogue (frsa_qkv_rope) + attention with
+    identity tables, against the same block on the unfused path (same weights):
+    output and the gradients of x, W_qkv and b_qkv."""
+    from triton_fused_rope_flash_attn_b200.block import RopeAttention
+    torch.manual_seed(1)
+    ref = RopeAttention(dim, heads, H_img=side, has_cls=has_cls, device="cuda",
+                        dtype=torch.bfloat16)
+    fused = RopeAttention(dim, heads, H_img=side, has_cls=has_cls, device="cuda",
+                          dtype=torch.bfloat16, fused_qkv=True)
+    fused.load_state_dict(ref.state_dict())
+    N = side * side + (1 if has_cls else 0)
+    x0 = torch.randn(2, N, dim, device="cuda", dtype=torch.bfloat16)
+    outs = []
+    for blk in (ref, fused):
+        x = x0.clone().requires_grad_(True)
+        y = blk(x)
+        y.backward(torch.ones_like(y))
+        outs.append((y.detach().float(), x.grad.float(), blk.qkv.weight.grad.float(),
+                     blk.qkv.bias.grad.float()))
+    for a, b in zip(*outs):
+        assert float((a - b).abs().max() / b.abs().max()) < 2e-2

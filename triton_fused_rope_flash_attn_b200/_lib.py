@@ -16,6 +16,7 @@ FRSA_DTYPE_F32 = 2
 
 EXPORTED_SYMBOLS = (
     "frsa_fwd",
+    "frsa_qkv_rope",
     "frsa_bwd",
     "frsa_bwd_workspace_bytes",
     "frsa_strerror",
@@ -57,6 +58,28 @@ class FrsaAttnArgs(ctypes.Structure):
     ]
 
 
+class FrsaQkvArgs(ctypes.Structure):
+    """Mirror of ``frsa_qkv_args`` (include/frsa.h)."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("w", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("cosp", ctypes.c_void_p),
+        ("sinp", ctypes.c_void_p),
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("B", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("n_pos", ctypes.c_int64),
+        ("has_cls", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
 class FrsaError(RuntimeError):
     """A non-zero status returned by the C ABI."""
 
@@ -91,6 +114,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.frsa_strerror.restype = ctypes.c_char_p
     lib.frsa_query_status.argtypes = []
     lib.frsa_query_status.restype = ctypes.c_int
+    lib.frsa_qkv_rope.argtypes = [ctypes.POINTER(FrsaQkvArgs), ctypes.c_void_p]
+    lib.frsa_qkv_rope.restype = ctypes.c_int
     lib.frsa_bwd_noalloc.argtypes = [ctypes.POINTER(FrsaAttnArgs), ctypes.c_void_p]
     lib.frsa_bwd_noalloc.restype = ctypes.c_int
     lib.frsa_bwd_noalloc_max_elements.argtypes = []

@@ -17,6 +17,7 @@
 #include "frsa_fwd.cu"
 #include "frsa_fwd_small.cu"
 #include "frsa_tf32.cu"
+#include "frsa_qkv.cu"
 
 namespace {
 
@@ -80,6 +81,22 @@ bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s,
                         3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
+  return r == CUDA_SUCCESS;
+}
+
+// 2-D map over a contiguous [rows, cols] 16-bit matrix, box {64, 128}.
+bool encode_map_2d(CUtensorMap* m, const void* base, long long rows, long long cols, bool bf16) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
   return r == CUDA_SUCCESS;
@@ -215,6 +232,33 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
 }
 
 const char* frsa_last_error_detail(void) { return g_last_detail; }
+
+int frsa_qkv_rope(const frsa_qkv_args* a, void* stream) {
+  if (!a || !a->x || !a->w || !a->bias || !a->cosp || !a->sinp || !a->q || !a->k || !a->v)
+    return FRSA_ERR_NULL_ARG;
+  if (a->B < 1 || a->N < 1 || a->H < 1 || a->C < 1 || a->C % a->H != 0) return FRSA_ERR_BAD_SHAPE;
+  if (a->has_cls != 0 && a->has_cls != 1) return FRSA_ERR_BAD_SHAPE;
+  if (a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;
+  const long long D = a->C / a->H;
+  if (a->C % 128 != 0 || D % 32 != 0 || D > 128) return FRSA_ERR_UNSUPPORTED_D;
+  if (a->dtype != FRSA_DTYPE_BF16 && a->dtype != FRSA_DTYPE_F16) return FRSA_ERR_UNSUPPORTED_DTYPE;
+  const long long M = a->B * a->N;
+  if ((M + 127) / 128 > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
+  if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->bias) || !aligned16(a->q) ||
+      !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) || !aligned16(a->sinp))
+    return FRSA_ERR_MISALIGNED;
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  (void)cudaGetLastError();
+  const bool bf16 = a->dtype == FRSA_DTYPE_BF16;
+  CUtensorMap tx, tw;
+  if (!encode_map_2d(&tx, a->x, M, a->C, bf16) || !encode_map_2d(&tw, a->w, 3 * a->C, a->C, bf16))
+    return launch_error("frsa_qkv_rope", cudaSuccess);
+  const cudaError_t e = frsa::launch_qkv_rope(
+      bf16, tx, tw, a->bias, a->cosp, a->sinp, a->q, a->k, a->v, M, static_cast<int>(a->N),
+      static_cast<int>(a->C), static_cast<int>(a->H), static_cast<int>(D),
+      static_cast<int>(a->has_cls), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : launch_error("frsa_qkv_rope", e);
+}
 
 #ifdef FRSA_TRACE
 // Trace builds only: copy the phase stamps (2048 CTAs x 64 slots) to `host`.

@@ -33,6 +33,13 @@ cudaError_t launch_fwd_tf32(const LaunchShape& s, const CUtensorMap& tm_q,
                             const CUtensorMap& tm_k, const CUtensorMap& tm_v, const float* cosp,
                             const float* sinp, float* o, float* lse, cudaStream_t stream);
 
+// QKV projection with RoPE in the epilogue (frsa_qkv.cu). tm_x: 2-D {C, M},
+// tm_w: 2-D {C, 3C}, both box {64, 128}, 128-byte swizzle.
+cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMap& tm_w,
+                            const float* bias, const float* cosp, const float* sinp, void* q,
+                            void* k, void* v, long long M, int N, int C, int H, int D,
+                            int has_cls, cudaStream_t stream);
+
 // Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
 bool fwd_small_applies(const LaunchShape& s);
 cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
