@@ -76,8 +76,9 @@ typedef struct frsa_attn_args {
   int64_t B, H, N, D, n_pos;
   int32_t has_cls;
   int32_t io_dtype;       /* enum frsa_dtype; must equal compute_dtype in this ABI version */
-  int32_t compute_dtype;  /* enum frsa_dtype: BF16 or F16; F32 (float32 tensors, TF32
-                             tensor-core products) for frsa_fwd only */
+  int32_t compute_dtype;  /* enum frsa_dtype: BF16 or F16; F32 = float32 tensors with
+                             TF32 tensor-core products (frsa_bwd: D <= 64, and a Delta
+                             workspace of B*H*N floats unless `delta` is given) */
   float scale;
 } frsa_attn_args;
 

@@ -110,11 +110,17 @@ def test_fwd_validation_before_device(lib, kw, code):
     assert lib.frsa_fwd(ctypes.byref(_args(**kw)), None) == code
 
 
-def test_bwd_float32_is_forward_only(lib):
+def test_bwd_float32_contract(lib):
+    # float32 backward: D <= 64, a Delta workspace of B*H*N floats unless delta is given.
     a = _args(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32)
     a.d_o = a.dq = a.dk = a.dv = 0x3000
-    assert lib.frsa_bwd(ctypes.byref(a), None) == 4
-    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(a)) == 0
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(a)) == 197 * 4
+    assert lib.frsa_bwd(ctypes.byref(a), None) == 9          # workspace missing
+    a.workspace, a.workspace_bytes = 0x4000, 197 * 4
+    assert lib.frsa_bwd(ctypes.byref(a), None) == 8          # no sm_100 device here
+    big = _args(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32, D=80, n_pos=196)
+    big.d_o = big.dq = big.dk = big.dv = 0x3000
+    assert lib.frsa_bwd(ctypes.byref(big), None) == 3        # D > 64: unsupported
 
 
 def test_bwd_requires_gradients_and_workspace(lib):

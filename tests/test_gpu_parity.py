@@ -206,3 +206,29 @@ def test_tf32_forward_against_oracle(side, has_cls, D):
     assert err < 5e-3, err
     assert np.abs(lse.double().cpu().numpy() - lse_ref).max() < 1e-2
 
+
+
+@pytest.mark.parametrize("side,has_cls,D", [(14, True, 64), (3, False, 64), (16, True, 64),
+                                            (6, True, 32), (24, False, 64)])
+def test_tf32_backward_against_oracle(side, has_cls, D):
+    """Native float32 backward (kind::tf32: Delta pass, dK/dV kernel, dQ kernel)
+    through the C ABI, against the float64 oracle; bar 5e-3 of each output's scale."""
+    from triton_fused_rope_flash_attn_b200 import (CosSinTable, fused_rope_attention_bwd,
+                                                   fused_rope_attention_fwd)
+    B, H = 2, 2
+    N = side * side + (1 if has_cls else 0)
+    q, k, v, do = seeded_inputs(B, H, N, D, 1.0, 23)
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    qd, kd, vd, dod = (t.cuda().float() for t in (q, k, v, do))
+    o, lse = fused_rope_attention_fwd(qd, kd, vd, cs.COSP, cs.SINP, has_cls)
+    dq, dk, dv = fused_rope_attention_bwd(qd, kd, vd, o, lse, dod, cs.COSP, cs.SINP, has_cls)
+    torch.cuda.synchronize()
+    from triton_fused_rope_flash_attn_b200 import _lib
+    assert _lib.load().frsa_query_status() == 0
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    refs = attn_bwd_np(q.double().numpy(), k.double().numpy(), v.double().numpy(),
+                       do.double().numpy(), cos, sin, has_cls)
+    for name, got, ref in zip(("dq", "dk", "dv"), (dq, dk, dv), refs):
+        assert got.dtype == torch.float32
+        err = np.abs(got.double().cpu().numpy() - ref).max() / np.abs(ref).max()
+        assert err < 5e-3, (name, err)

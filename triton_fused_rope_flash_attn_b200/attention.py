@@ -124,13 +124,14 @@ def _pow2_normaliser(x: torch.Tensor, target: float = 1.0) -> float:
 
 # float32 compute. The reference computes fp32 inputs with Triton's TF32 dot
 # products (10-bit mantissa operands, fp32 accumulation; fa_rope_full .py:65-73
-# selects float32 as the kernel dtype). The forward here is the native
-# kind::tf32 kernel (fp32 in and out). The backward runs on the f16 kernels,
-# whose operands have the same 10-bit mantissa as TF32, with accumulation in
-# fp32; f16's narrower exponent range is handled exactly: each operand is
-# multiplied by a power of two that brings its largest magnitude to 1 (dO to
-# 1/8, leaving headroom for dV = P^T dO and dQ = dS K), the logit scale absorbs
-# the Q and K factors, and the gradients are divided back and returned in fp32.
+# selects float32 as the kernel dtype). Here the forward, and the backward for
+# D <= 64, are native kind::tf32 kernels (fp32 in and out). For D > 64 the
+# backward runs on the f16 kernels, whose operands have the same 10-bit
+# mantissa as TF32, with accumulation in fp32; f16's narrower exponent range is
+# handled exactly: each operand is multiplied by a power of two that brings its
+# largest magnitude to 1 (dO to 1/8, leaving headroom for dV = P^T dO and
+# dQ = dS K), the logit scale absorbs the Q and K factors, and the gradients
+# are divided back and returned in fp32.
 def _fp32_forward(Q, K, V, COSP, SINP, has_cls):
     return fused_rope_attention_fwd(Q.contiguous(), K.contiguous(), V.contiguous(), COSP, SINP,
                                     has_cls)
@@ -138,6 +139,8 @@ def _fp32_forward(Q, K, V, COSP, SINP, has_cls):
 
 def _fp32_backward(Q, K, V, O, lse, dO, COSP, SINP, has_cls):
     D = Q.shape[-1]
+    if D <= 64:
+        return fused_rope_attention_bwd(Q, K, V, O, lse, dO.contiguous(), COSP, SINP, has_cls)
     sq, sk, sv = _pow2_normaliser(Q), _pow2_normaliser(K), _pow2_normaliser(V)
     sd = _pow2_normaliser(dO, 0.125)
     qh, kh, vh = (Q * sq).half(), (K * sk).half(), (V * sv).half()

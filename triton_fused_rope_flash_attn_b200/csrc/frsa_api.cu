@@ -144,6 +144,35 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   return FRSA_OK;
 }
 
+// float32 backward (TF32 tensor cores), D <= 64.
+int bwd_f32(const frsa_attn_args* a, const frsa::LaunchShape& s, void* stream) {
+  if (!frsa::tf32_bwd_supported(s)) return FRSA_ERR_UNSUPPORTED_D;
+  if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv) return FRSA_ERR_NULL_ARG;
+  if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||
+      !aligned16(a->dv) || !aligned16(a->lse))
+    return FRSA_ERR_MISALIGNED;
+  float* delta = a->delta;
+  if (delta == nullptr) {
+    const size_t need = static_cast<size_t>(s.BH) * s.N * sizeof(float);
+    if (!a->workspace || a->workspace_bytes < need) return FRSA_ERR_WORKSPACE;
+    delta = static_cast<float*>(a->workspace);
+  }
+  if (!aligned16(delta)) return FRSA_ERR_MISALIGNED;
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  (void)cudaGetLastError();
+  CUtensorMap maps[7];   // q16, q32, k16, k32, v16, do16, do32
+  if (!encode_map(&maps[0], a->q, s) || !encode_map(&maps[1], a->q, s, true) ||
+      !encode_map(&maps[2], a->k, s) || !encode_map(&maps[3], a->k, s, true) ||
+      !encode_map(&maps[4], a->v, s) || !encode_map(&maps[5], a->d_o, s) ||
+      !encode_map(&maps[6], a->d_o, s, true))
+    return launch_error("frsa_bwd", cudaSuccess);
+  const cudaError_t e = frsa::launch_bwd_tf32(
+      s, maps, static_cast<const float*>(a->o), static_cast<const float*>(a->d_o), a->lse, delta,
+      a->cosp, a->sinp, static_cast<float*>(a->dq), static_cast<float*>(a->dk),
+      static_cast<float*>(a->dv), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -172,7 +201,8 @@ const char* frsa_strerror(int code) {
 size_t frsa_bwd_workspace_bytes(const frsa_attn_args* a) {
   frsa::LaunchShape s;
   if (validate_common(a, &s) != FRSA_OK) return 0;
-  if (s.f32) return 0;   // no float32 backward through this ABI
+  if (s.f32)   // Delta scratch of the float32 backward (unless args->delta is given)
+    return frsa::tf32_bwd_supported(s) ? static_cast<size_t>(s.BH) * s.N * sizeof(float) : 0;
   if (!frsa::bwd_needs_workspace(s)) return 0;
   return static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
 }
@@ -203,7 +233,7 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
   frsa::LaunchShape s;
   int rc = validate_common(a, &s);
   if (rc != FRSA_OK) return rc;
-  if (s.f32) return FRSA_ERR_UNSUPPORTED_DTYPE;   // float32: forward only
+  if (s.f32) return bwd_f32(a, s, stream);
   if (!a->o || !a->lse || !a->d_o || !a->dq || !a->dk || !a->dv)
     return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||

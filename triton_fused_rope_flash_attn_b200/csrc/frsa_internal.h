@@ -33,6 +33,16 @@ cudaError_t launch_fwd_tf32(const LaunchShape& s, const CUtensorMap& tm_q,
                             const CUtensorMap& tm_k, const CUtensorMap& tm_v, const float* cosp,
                             const float* sinp, float* o, float* lse, cudaStream_t stream);
 
+// float32 backward on TF32 tensor cores (D <= 64): a Delta pass into `delta`
+// (fp32 [BH, N]), a dK/dV kernel and a dQ kernel. maps: q, k, v, dO in the
+// K-major layout and q, k, dO in the MN-major (32-byte-atom) layout, in the
+// order q16, q32, k16, k32, v16, do16, do32.
+bool tf32_bwd_supported(const LaunchShape& s);
+cudaError_t launch_bwd_tf32(const LaunchShape& s, const CUtensorMap* maps, const float* o,
+                            const float* d_o, const float* lse, float* delta, const float* cosp,
+                            const float* sinp, float* dq, float* dk, float* dv,
+                            cudaStream_t stream);
+
 // QKV projection with RoPE in the epilogue (frsa_qkv.cu). tm_x: 2-D {C, M},
 // tm_w: 2-D {C, 3C}, both box {64, 128}, 128-byte swizzle.
 cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMap& tm_w,
