@@ -273,7 +273,8 @@ int frsa_qkv_rope(const frsa_qkv_args* a, void* stream) {
   if (a->C % 128 != 0 || D % 32 != 0 || D > 128) return FRSA_ERR_UNSUPPORTED_D;
   if (a->dtype != FRSA_DTYPE_BF16 && a->dtype != FRSA_DTYPE_F16) return FRSA_ERR_UNSUPPORTED_DTYPE;
   const long long M = a->B * a->N;
-  if ((M + 127) / 128 > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
+  if ((M + 127) / 128 * (3 * a->C / 128) > 0x7FFFFFFFLL || a->N > (1LL << 30))
+    return FRSA_ERR_BAD_SHAPE;
   if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->bias) || !aligned16(a->q) ||
       !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) || !aligned16(a->sinp))
     return FRSA_ERR_MISALIGNED;

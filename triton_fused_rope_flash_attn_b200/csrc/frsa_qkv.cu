@@ -10,11 +10,16 @@
 // rotated here, the attention runs with identity tables, so the rotation
 // leaves the attention kernels' critical path.
 //
-// One CTA per 128 x 128 output tile: warp 0 streams x and W tiles (128 rows x
-// 64 columns, 128-byte swizzle) through a 3-stage TMA ring, warp 1 issues
-// tcgen05.mma (M = 128 tokens, N = 128 features, K16 steps, f32 accumulator in
-// TMEM), warps 4-7 run the epilogue (thread = token row = TMEM lane). A tile
-// of 128 features is two heads of one of q, k, v when C and D divide 128.
+// Persistent: one CTA per SM walks 128 x 128 output tiles (token tile major,
+// so consecutive CTAs reuse a token tile of x from L2). Warp 0 streams x and W
+// tiles (128 rows x 64 columns, 128-byte swizzle) through a 4-stage TMA ring;
+// warp 1 issues tcgen05.mma (M = 128 tokens, N = 128 features, K16 steps)
+// into one of two TMEM accumulators; warps 4-7 run the epilogue of the other
+// accumulator (thread = token row = TMEM lane), so a tile's epilogue overlaps
+// the next tile's products. Warps 4-7 and 8-11 are two epilogue groups, each
+// taking two of the four 32-column groups of every 128 columns. A tile of 128 features lies within one of q, k, v
+// when C divides by 128, and 32-column groups lie within one head when D
+// divides by 32.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 
@@ -22,13 +27,15 @@ namespace frsa {
 
 namespace {
 
-constexpr int kQkvThreads = 256;
-constexpr int kQkvStages = 3;
+constexpr int kQkvThreads = 384;
+constexpr int kQkvStages = 4;
 
+template <int BN>
 struct QkvSmem {
-  uint8_t a[kQkvStages][kChunkBytes];   // x tile: 128 tokens x 64 channels
-  uint8_t b[kQkvStages][kChunkBytes];   // W tile: 128 features x 64 channels
-  uint64_t full[kQkvStages], empty[kQkvStages], acc_full;
+  uint8_t a[kQkvStages][kChunkBytes];             // x tile: 128 tokens x 64 channels
+  uint8_t b[kQkvStages][BN / kTile][kChunkBytes];  // W tile: BN features x 64 channels
+  uint64_t full[kQkvStages], empty[kQkvStages];
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -41,20 +48,20 @@ struct QkvParams {
   void* k;
   void* v;
   long long M;         // B * N tokens
-  int N, C, H, D, has_cls, kblocks;
+  int N, C, H, D, has_cls, kblocks, nft, ntiles;
 };
 
-template <typename T>
+template <typename T, int BN>
 __global__ void __launch_bounds__(kQkvThreads, 1)
     qkv_rope_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w, const QkvParams prm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  QkvSmem* smp = aligned_smem<QkvSmem>(smem_raw);
+  QkvSmem<BN>* smp = aligned_smem<QkvSmem<BN>>(smem_raw);
   if (smp == nullptr) return;
-  QkvSmem& sm = *smp;
+  QkvSmem<BN>& sm = *smp;
+  constexpr int NB = BN / kTile;   // 128-row W boxes per tile
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int mt = blockIdx.x, ft = blockIdx.y;   // token tile, feature tile
   const int nk = prm.kblocks;
   volatile int* abort_flag = &sm.abort_flag;
 
@@ -64,11 +71,14 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.acc_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.acc_full[s], 1);
+      mbar_init(&sm.acc_empty[s], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&sm.tmem_base, 128);
+    tmem_alloc(&sm.tmem_base, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -80,77 +90,120 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_w);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kQkvStages;
-        mbar_wait(&sm.empty[s], ((kb / kQkvStages) & 1) ^ 1, abort_flag);
-        mbar_arrive_expect_tx(&sm.full[s], 2 * kChunkBytes);
-        tma_load_2d(sm.a[s], &tm_x, &sm.full[s], kb * 64, mt * kTile);
-        tma_load_2d(sm.b[s], &tm_w, &sm.full[s], kb * 64, ft * kTile);
+      int kc = 0;   // running k-block count (ring position)
+      for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x) {
+        const int mt = t / prm.nft, ft = t - mt * prm.nft;
+        for (int kb = 0; kb < nk; ++kb, ++kc) {
+          const int s = kc % kQkvStages;
+          mbar_wait(&sm.empty[s], ((kc / kQkvStages) & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.full[s], (1 + NB) * kChunkBytes);
+          tma_load_2d(sm.a[s], &tm_x, &sm.full[s], kb * 64, mt * kTile);
+          for (int h = 0; h < NB; ++h)
+            tma_load_2d(sm.b[s][h], &tm_w, &sm.full[s], kb * 64, ft * BN + h * kTile);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t id = idesc_f16(Elt<T>::kBf16, 128, 128, false, false);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kQkvStages;
-        mbar_wait(&sm.full[s], (kb / kQkvStages) & 1, abort_flag);
+      const uint32_t id = idesc_f16(Elt<T>::kBf16, 128, BN, false, false);
+      int kc = 0, tl = 0;
+      for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++tl) {
+        const int ab = tl & 1;   // accumulator buffer
+        mbar_wait(&sm.acc_empty[ab], ((tl >> 1) & 1) ^ 1, abort_flag);
         tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb, ++kc) {
+          const int s = kc % kQkvStages;
+          mbar_wait(&sm.full[s], (kc / kQkvStages) & 1, abort_flag);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ss(tmem, sw128_desc(smem_u32(sm.a[s]) + kk * 32, 16, 1024),
-                 sw128_desc(smem_u32(sm.b[s]) + kk * 32, 16, 1024), id, (kb | kk) != 0);
-        mma_commit(&sm.empty[s]);   // stage s free once these products have read it
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ss(tmem + BN * ab, sw128_desc(smem_u32(sm.a[s]) + kk * 32, 16, 1024),
+                   sw128_desc(smem_u32(sm.b[s][0]) + kk * 32, 16, 1024), id, (kb | kk) != 0);
+          mma_commit(&sm.empty[s]);   // stage s free once these products have read it
+        }
+        mma_commit(&sm.acc_full[ab]);
       }
-      mma_commit(&sm.acc_full);
     }
   } else if (warp >= 4) {
-    // Epilogue: thread = token row r of the tile = TMEM lane.
+    // Epilogue: thread = token row r of the tile = TMEM lane. tcgen05.ld is
+    // warp-collective: every lane loads; only rows that are tokens are stored.
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const long long m = static_cast<long long>(mt) * kTile + r;
-    mbar_wait(&sm.acc_full, 0, abort_flag);
-    tc_fence_after();
-    // tcgen05.ld is warp-collective: every lane loads; only rows that are
-    // tokens (m < M) are stored.
-    const bool valid = m < prm.M;
+    const bool leader = threadIdx.x == 128;
+    const int eg = (warp - 4) >> 2;   // epilogue group: 32-column groups 2 eg, 2 eg + 1
     const int C = prm.C, D = prm.D, N = prm.N;
-    const long long mm = valid ? m : 0;
-    const int b = static_cast<int>(mm / N), n = static_cast<int>(mm - static_cast<long long>(b) * N);
-    const int f0 = ft * kTile;
-    const int which = f0 / C;                  // 0 q, 1 k, 2 v
-    const bool rot = which < 2;
-    const int pos = (prm.has_cls && n == 0) ? -1 : n - prm.has_cls;
-    T* dstbase = static_cast<T*>(which == 0 ? prm.q : which == 1 ? prm.k : prm.v);
     const int D2 = D >> 1;
+    int tl = 0;
+    for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++tl) {
+      const int ab = tl & 1;
+      const int mt = t / prm.nft, ft = t - mt * prm.nft;
+      const long long m = static_cast<long long>(mt) * kTile + r;
+      const bool valid = m < prm.M;
+      const long long mm = valid ? m : 0;
+      const int b = static_cast<int>(mm / N), n = static_cast<int>(mm - static_cast<long long>(b) * N);
+      const int f0 = ft * BN;
+      const int which = f0 / C;                  // 0 q, 1 k, 2 v
+      const bool rot = which < 2;
+      const int pos = (prm.has_cls && n == 0) ? -1 : n - prm.has_cls;
+      T* dstbase = static_cast<T*>(which == 0 ? prm.q : which == 1 ? prm.k : prm.v);
+      mbar_wait(&sm.acc_full[ab], (tl >> 1) & 1, abort_flag);
+      tc_fence_after();
 #pragma unroll 1
-    for (int c32 = 0; c32 < 4; ++c32) {
-      float v[32];
-      tmem_ld32(tmem + lane_off + 32 * c32, v);
-      tmem_wait_ld();
-      if (!valid) continue;
-      const int fc = f0 + 32 * c32;            // first feature of these 32
-      const int h = (fc % C) / D, d0 = fc % D; // head and first head-dim index
+      for (int hb = 0; hb < NB; ++hb) {
+        float v[2][32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] += __ldg(prm.bias + fc + e);
-      if (rot && pos >= 0) {
-        const float* cr = prm.cosp + static_cast<size_t>(pos) * D2 + (d0 >> 1);
-        const float* sr = prm.sinp + static_cast<size_t>(pos) * D2 + (d0 >> 1);
-#pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float c = __ldg(cr + p), s = __ldg(sr + p);
-          const float e0 = v[2 * p], o0 = v[2 * p + 1];
-          v[2 * p] = e0 * c - o0 * s;
-          v[2 * p + 1] = o0 * c + e0 * s;
+        for (int c = 0; c < 2; ++c)
+          tmem_ld32(tmem + BN * ab + lane_off + 128 * hb + 32 * (2 * eg + c), v[c]);
+        tmem_wait_ld();
+        if (hb == NB - 1) {
+          // Accumulator read: the next tile's products may overwrite it.
+          tc_fence_before();
+          named_bar(1, 256);
+          if (leader) mbar_arrive(&sm.acc_empty[ab]);
         }
-      }
-      T* dst = dstbase + ((static_cast<size_t>(b) * prm.H + h) * N + n) * D + d0;
+        if (!valid) continue;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint32_t w[4];
+        for (int c32 = 0; c32 < 2; ++c32) {
+          const int fc = f0 + 128 * hb + 32 * (2 * eg + c32);  // first feature of these 32
+          const int h = (fc % C) / D, d0 = fc % D;  // head and first head-dim index
+          const float4* bias4 = reinterpret_cast<const float4*>(prm.bias + fc);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = Elt<T>::pack(v[8 * g + 2 * e], v[8 * g + 2 * e + 1]);
-        reinterpret_cast<uint4*>(dst)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 bb = __ldg(bias4 + e4);
+            v[c32][4 * e4] += bb.x;
+            v[c32][4 * e4 + 1] += bb.y;
+            v[c32][4 * e4 + 2] += bb.z;
+            v[c32][4 * e4 + 3] += bb.w;
+          }
+          if (rot && pos >= 0) {
+            const float4* cr =
+                reinterpret_cast<const float4*>(prm.cosp + static_cast<size_t>(pos) * D2 + (d0 >> 1));
+            const float4* sr =
+                reinterpret_cast<const float4*>(prm.sinp + static_cast<size_t>(pos) * D2 + (d0 >> 1));
+#pragma unroll
+            for (int p4 = 0; p4 < 4; ++p4) {
+              const float4 c4 = __ldg(cr + p4), s4 = __ldg(sr + p4);
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int p = 4 * p4 + q;
+                const float e0 = v[c32][2 * p], o0 = v[c32][2 * p + 1];
+                v[c32][2 * p] = e0 * cc[q] - o0 * ss[q];
+                v[c32][2 * p + 1] = o0 * cc[q] + e0 * ss[q];
+              }
+            }
+          }
+          T* dst = dstbase + ((static_cast<size_t>(b) * prm.H + h) * N + n) * D + d0;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = Elt<T>::pack(v[c32][8 * g + 2 * e], v[c32][8 * g + 2 * e + 1]);
+            reinterpret_cast<uint4*>(dst)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
       }
     }
   }
@@ -159,7 +212,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
@@ -183,22 +236,27 @@ cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMa
   p.D = D;
   p.has_cls = has_cls;
   p.kblocks = C / 64;
-  const size_t smem = sizeof(QkvSmem) + 1024;
-  const dim3 grid(static_cast<unsigned>((M + kTile - 1) / kTile), static_cast<unsigned>(3 * C / kTile));
-  if (bf16) {
-    auto kern = qkv_rope_kernel<__nv_bfloat16>;
+  // 128 x 256 tiles when a tile of 256 features stays within one of q, k, v.
+  const int BN = (C % 256 == 0) ? 256 : 128;
+  p.nft = 3 * C / BN;
+  const long long ntiles = ((M + kTile - 1) / kTile) * p.nft;
+  p.ntiles = static_cast<int>(ntiles);
+  int nsm = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const dim3 grid(static_cast<unsigned>(ntiles < nsm ? ntiles : nsm));
+  auto launch = [&](auto kern, size_t smem) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kern<<<grid, kQkvThreads, smem, stream>>>(tm_x, tm_w, p);
-  } else {
-    auto kern = qkv_rope_kernel<__half>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    kern<<<grid, kQkvThreads, smem, stream>>>(tm_x, tm_w, p);
-  }
-  return cudaGetLastError();
+    return cudaGetLastError();
+  };
+  if (BN == 256)
+    return bf16 ? launch(qkv_rope_kernel<__nv_bfloat16, 256>, sizeof(QkvSmem<256>) + 1024)
+                : launch(qkv_rope_kernel<__half, 256>, sizeof(QkvSmem<256>) + 1024);
+  return bf16 ? launch(qkv_rope_kernel<__nv_bfloat16, 128>, sizeof(QkvSmem<128>) + 1024)
+              : launch(qkv_rope_kernel<__half, 128>, sizeof(QkvSmem<128>) + 1024);
 }
 
 }  // namespace frsa
