@@ -191,14 +191,14 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       mbar_wait(&sm.q_full[st], hp, abort_flag);
       for (int g = 0; g < nqt; ++g)
         for (int rr = t; rr < kTile; rr += 64)
-          rotate_row_t<T>(smem_u32(sm.q[st][g]), smem_u32(sm.tab[g]), rr, D);
+          rotate_row_t<T, 4>(smem_u32(sm.q[st][g]), smem_u32(sm.tab[g]), rr, D);
       fence_proxy_async_smem();
       named_bar(1, 64);
       if (t == 0) mbar_arrive(&sm.q_ready[st]);
       for (int j = 0; j < nkv; ++j) {
         mbar_wait(&sm.kv_full[st][j], hp, abort_flag);
         for (int rr = t; rr < kTile; rr += 64)
-          rotate_row_t<T>(smem_u32(sm.k[st][j]), smem_u32(sm.tab[j]), rr, D);
+          rotate_row_t<T, 4>(smem_u32(sm.k[st][j]), smem_u32(sm.tab[j]), rr, D);
         fence_proxy_async_smem();
         named_bar(1, 64);
         if (t == 0) mbar_arrive(&sm.k_ready[st][j]);

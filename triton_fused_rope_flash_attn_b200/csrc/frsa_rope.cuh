@@ -256,23 +256,37 @@ __device__ __forceinline__ void store_tabrow(uint32_t tab, int r, int pos, int D
   }
 }
 
-// Rotate row r of a one-chunk tile in place with table tile `tab`.
-template <typename T>
+// Rotate row r of a one-chunk tile in place with table tile `tab`, kBatch
+// granules at a time: with kBatch > 1 all of a batch's shared loads are issued
+// before its first store (the loads and stores are ordered asm), so their
+// latencies overlap, at the cost of 8 registers per granule in flight.
+template <typename T, int kBatch = 1>
 __device__ __forceinline__ void rotate_row_t(uint32_t tile, uint32_t tab, int r, int D) {
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    if (8 * g < D) {
-      const uint4 x = lds_u4(tile + sw128_off(r, g));
-      const uint4 t = lds_u4(tab + sw128_off(r, g));
-      const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, tw[4] = {t.x, t.y, t.z, t.w};
-      uint32_t w[4];
+  for (int g0 = 0; g0 < 8; g0 += kBatch) {
+    if (8 * g0 >= D) break;
+    uint4 x[kBatch], t[kBatch];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 cs = Elt<__half>::unpack(tw[e]);
-        const float2 v = Elt<T>::unpack(xw[e]);
-        w[e] = Elt<T>::pack(v.x * cs.x - v.y * cs.y, v.y * cs.x + v.x * cs.y);
+    for (int k = 0; k < kBatch; ++k) {
+      if (8 * (g0 + k) < D) {
+        x[k] = lds_u4(tile + sw128_off(r, g0 + k));
+        t[k] = lds_u4(tab + sw128_off(r, g0 + k));
       }
-      sts_u4(tile + sw128_off(r, g), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      if (8 * (g0 + k) < D) {
+        const uint32_t xw[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
+        const uint32_t tw[4] = {t[k].x, t[k].y, t[k].z, t[k].w};
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 cs = Elt<__half>::unpack(tw[e]);
+          const float2 v = Elt<T>::unpack(xw[e]);
+          w[e] = Elt<T>::pack(v.x * cs.x - v.y * cs.y, v.y * cs.x + v.x * cs.y);
+        }
+        sts_u4(tile + sw128_off(r, g0 + k), make_uint4(w[0], w[1], w[2], w[3]));
+      }
     }
   }
 }
