@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
         mbar_init(&sm.kv_empty[s][j], 1);
       }
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], 1);
+      mbar_init(&sm.p_full[s], 4);   // one arrival per softmax warp
       mbar_init(&sm.o_full[s], 1);
     }
     fence_mbar_init();
@@ -294,8 +294,9 @@ __global__ void __launch_bounds__(kFsThreads, 1)
             m2 = m_new;
           }
           tc_fence_before();
-          named_bar(2 + g, 128);
-          if (leader) mbar_arrive(&sm.p_full[g]);
+          // Each warp publishes its own rows (no cross-warp barrier here).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_full[g]);
 
           mbar_wait(&sm.o_full[g], c & 1, abort_flag);
           tc_fence_after();
