@@ -407,7 +407,7 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
 cudaError_t launch_fwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                        const CUtensorMap& tm_v, const CUtensorMap& tm_o, const float* cosp,
                        const float* sinp, void* o, float* lse, cudaStream_t stream) {
-  if (fwd_small_applies(s)) return launch_fwd_small(s, tm_q, tm_k, tm_v, tm_o, cosp, sinp, lse, stream);
+  if (fwd_small_applies(s)) return launch_fwd_small(s, tm_q, tm_k, tm_v, cosp, sinp, o, lse, stream);
   const bool two = s.D > 64;
   if (s.bf16) {
     return two ? launch_fwd_t<__nv_bfloat16, 2>(s, tm_q, tm_k, tm_v, cosp, sinp, o, lse, stream)

@@ -54,8 +54,8 @@ cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMa
 bool fwd_small_applies(const LaunchShape& s);
 cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
                              const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                             const CUtensorMap& tm_o, const float* cosp, const float* sinp,
-                             float* lse, cudaStream_t stream);
+                             const float* cosp, const float* sinp, void* o, float* lse,
+                             cudaStream_t stream);
 
 // Persistent backward for N <= 256, D <= 64 (dQ reduced on chip).
 cudaError_t launch_bwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
