@@ -36,6 +36,7 @@ CASES = [
     (1, 3, 16, True, 64, 1.0, torch.bfloat16),    # N=257 (atomic-dQ path)
     (1, 2, 24, False, 64, 1.0, torch.bfloat16),   # N=576 (ViT-L)
     (1, 2, 14, True, 32, 1.0, torch.bfloat16),    # D=32
+    (1, 2, 15, True, 48, 1.0, torch.bfloat16),    # D=48, N=226 (240 computed keys)
     (1, 2, 7, True, 80, 1.0, torch.bfloat16),     # D=80, N=50
     (1, 2, 14, True, 128, 1.0, torch.bfloat16),   # D=128
 ]
@@ -84,9 +85,13 @@ def test_fwd_bwd_parity(case):
     assert mx <= 1e-2, f"lse max abs err {mx:.3e}"
 
 
-def test_vit_h_like_relative():
-    """N=1370, D=80, inputs x2.0: relative mean error <= 1e-2 on every tensor."""
-    got, ref = _run(1, 2, 37, True, 80, 2.0, torch.bfloat16)
+@pytest.mark.parametrize("side,D", [(37, 80), (14, 64)])
+def test_amplified_inputs_relative(side, D):
+    """Inputs x2.0 (logits 4x wider, a peaked softmax): N=1370, D=80 (ViT-H
+    like, general kernels) and N=197, D=64 (persistent kernels). The bf16
+    rounding of the wider logits and outputs exceeds the absolute bar, so the
+    bar is a relative mean error <= 1e-2 on every tensor."""
+    got, ref = _run(1, 2, side, True, D, 2.0, torch.bfloat16)
     for name in ("o", "dq", "dk", "dv"):
         assert np.isfinite(got[name]).all(), name
         assert rel_err(got[name], ref[name]) <= 1e-2, name
