@@ -47,7 +47,7 @@ struct FsSmem {
   uint64_t q_full[2], q_ready[2], q_empty[2];
   uint64_t k_full[2], k_ready[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  uint64_t s_full[2], p_hi[2], p_full[2], o_full[2], o_free[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(kFsThreads, 1)
   const int DP = (D + 15) & ~15;
   const int ksteps = DP >> 4;
   const int nk16 = (N + 15) & ~15;   // key columns the products compute
+  // P of keys [128, nk16) fits past the scores (nk16 + (nk16 - 128) / 2 <= 256).
+  const bool split = nk16 > kTile && nk16 <= 208;
   const int nqt = prm.nqt, nkv = prm.nkv;
   volatile int* abort_flag = &sm.abort_flag;
 
@@ -92,7 +94,8 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       mbar_init(&sm.v_full[s], 1);
       mbar_init(&sm.v_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], 4);   // one arrival per softmax warp
+      mbar_init(&sm.p_hi[s], 4);     // one arrival per softmax warp
+      mbar_init(&sm.p_full[s], 4);
       mbar_init(&sm.o_full[s], 1);
       mbar_init(&sm.o_free[s], 4);
     }
@@ -167,13 +170,27 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       // last product of a head releases its K/V stage.
       auto issue_pv = [&](int g, int hl) {
         const int st = hl & 1;
-        mbar_wait(&sm.p_full[g], hl & 1, abort_flag);
         if (g == 0) mbar_wait(&sm.v_full[st], (hl >> 1) & 1, abort_flag);
-        tc_fence_after();
+        int ks0 = 0;
+        if (split) {
+          // Keys [128, nk16) first: their P sits past the scores.
+          mbar_wait(&sm.p_hi[g], hl & 1, abort_flag);
+          tc_fence_after();
 #pragma unroll 1
-        for (int ks = 0; ks < pvsteps; ++ks)
+          for (int ks = 8; ks < pvsteps; ++ks)
+            mma_ts(tmem + 256 * g + 128, tmem + 256 * g + nk16 + (ks - 8) * 8,
+                   sw128_desc(smem_u32(sm.v[st][0]) + ks * 2048, kChunkBytes, 1024), idO,
+                   ks > 8);
+          ks0 = 1;
+        }
+        mbar_wait(&sm.p_full[g], hl & 1, abort_flag);
+        tc_fence_after();
+        const int kend = split ? 8 : pvsteps;
+#pragma unroll 1
+        for (int ks = 0; ks < kend; ++ks)
           mma_ts(tmem + 256 * g + 128, tmem + 256 * g + ks * 8,
-                 sw128_desc(smem_u32(sm.v[st][0]) + ks * 2048, kChunkBytes, 1024), idO, ks > 0);
+                 sw128_desc(smem_u32(sm.v[st][0]) + ks * 2048, kChunkBytes, 1024), idO,
+                 ks + ks0 > 0);
         mma_commit(&sm.o_full[g]);
         if (g == nqt - 1) mma_commit(&sm.v_empty[st]);
       };
@@ -244,7 +261,6 @@ __global__ void __launch_bounds__(kFsThreads, 1)
     if (g < nqt) {
       int hl = 0;
       for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
-        const int st = hl & 1;
         mbar_wait(&sm.s_full[g], hl & 1, abort_flag);
         tc_fence_after();
         float m2 = 0.f, l = 1.f;
@@ -271,8 +287,12 @@ __global__ void __launch_bounds__(kFsThreads, 1)
           }
           m2 = mx * c2;
           float sum = 0.f;
+          // Split: the 64-key steps past key 128 go first and their P goes to
+          // columns [nk16, ...), past the scores, so P V can start on them
+          // while keys [0, 128) are processed (then published by p_full).
 #pragma unroll 1
-          for (int h = 0; h < npair; ++h) {
+          for (int hh = 0; hh < npair; ++hh) {
+            const int h = split ? (hh < npair - 2 ? hh + 2 : hh - (npair - 2)) : hh;
             float sv[2][32];
             tmem_ld32(tS + h * 64, sv[0]);
             tmem_ld32(tS + h * 64 + 32, sv[1]);
@@ -280,6 +300,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int cbase = h * 64 + u * 32;
+              if (split && cbase >= nk16) continue;
               uint32_t pk[16];
               if (cbase + 32 <= N) {
 #pragma unroll
@@ -300,12 +321,23 @@ __global__ void __launch_bounds__(kFsThreads, 1)
                 }
               }
               // P columns [cbase, cbase + 32) -> packed TMEM columns from
-              // cbase / 2 (already read: the write front trails the read front).
-              tmem_st16(tS + cbase / 2, pk);
+              // cbase / 2 (already read: the write front trails the read front),
+              // or from nk16 + (cbase - 128) / 2 for the split's high keys.
+              tmem_st16(tS + (split && cbase >= kTile ? nk16 + (cbase - kTile) / 2 : cbase / 2),
+                        pk);
+            }
+            if (split && hh == npair - 3) {
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sm.p_hi[g]);
             }
           }
           tmem_wait_st();
           l = sum;
+        } else if (split) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_hi[g]);
         }
         tc_fence_before();
         // Each warp publishes its own rows (no cross-warp barrier here).
