@@ -9,18 +9,21 @@
 //   warp 0      TMA producer: the two Q tiles once, then K/V tiles into a
 //               ring of KS stages
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..3  rotation warps: apply RoPE in shared memory to the Q tiles and
-//               to every K tile as soon as TMA has landed it
+//   warps 2..3, 12..13  rotation warps: apply RoPE in shared memory to the Q
+//               tiles and to every K tile as soon as TMA has landed it
 //   warps 4..11 two compute warpgroups, warpgroup g owns query tile g of the
 //               pair: it reads S from TMEM (thread = query row), writes P
-//               (16-bit) to its own shared tile, accumulates O in registers
-//               from the per-tile P V product, and writes O and the
-//               log-sum-exp. The MMA issue order (P_0 V, S_0 next, P_1 V,
-//               S_1 next) lets the two groups run out of phase, so one's
-//               softmax overlaps the other's MMAs.
+//               (16-bit) to its shared P buffers (two when D <= 64, so the
+//               next tile's softmax does not wait for this tile's P V), and
+//               writes O and the log-sum-exp. O accumulates in TMEM; the
+//               softmax base is raised (and O rescaled in TMEM) only when a
+//               tile's maximum exceeds it by more than 2^8. The MMA issue
+//               order (S_0 next, P_0 V, S_1 next, P_1 V) lets the two groups
+//               run out of phase and each group's next softmax overlap its
+//               own P V.
 //
 // TMEM columns: warpgroup g uses [256 g, 256 g + 128) for S and
-// [256 g + 128, 256 g + 128 + DP) for the per-tile P V.
+// [256 g + 128, 256 g + 128 + DP) for O.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
@@ -33,16 +36,18 @@ namespace frsa {
 namespace {
 
 constexpr int kFwdCompute = 256;                // two warpgroups
-constexpr int kFwdThreads = 128 + kFwdCompute;  // + producer, MMA and two rotation warps
+constexpr int kFwdThreads = 128 + kFwdCompute + 64;  // + producer, MMA, four rotation warps
 constexpr uint32_t kTmemColsFwd = 512;
+constexpr float kFwdSlack = 8.f;   // log2 headroom of the softmax base
 
 template <int NCH>
 struct FwdSmem {
   static constexpr int KS = (NCH == 1) ? 2 : 1;  // K/V ring stages
+  static constexpr int PB = (NCH == 1) ? 2 : 1;  // P buffers per warpgroup
   uint8_t q[2][NCH][kChunkBytes];      // query tile of warpgroup g
   uint8_t k[KS][NCH][kChunkBytes];     // key ring
   uint8_t v[KS][NCH][kChunkBytes];     // value ring
-  uint8_t p[2][2][kChunkBytes];        // P tile of warpgroup g: [128 q][128 kv], two chunks
+  uint8_t p[2][PB][2][kChunkBytes];    // P tiles of warpgroup g: [128 q][128 kv], two chunks
   uint64_t q_full[2];
   uint64_t q_ready;
   uint64_t kv_full[KS];
@@ -50,7 +55,7 @@ struct FwdSmem {
   uint64_t k_ready[KS];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_full[2];
+  uint64_t o_full[2][PB];              // P V of a tile using P buffer b has completed
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -70,6 +75,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
   using Sm = FwdSmem<NCH>;
   constexpr int KS = Sm::KS;
+  constexpr int PB = Sm::PB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Sm* smp = aligned_smem<Sm>(smem_raw);
   if (smp == nullptr) return;
@@ -91,7 +97,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&sm.q_full[s], 1);
       mbar_init(&sm.s_full[s], 1);
       mbar_init(&sm.p_full[s], 1);
-      mbar_init(&sm.o_full[s], 1);
+      for (int b = 0; b < Sm::PB; ++b) mbar_init(&sm.o_full[s][b], 1);
     }
     mbar_init(&sm.q_ready, 1);
     for (int s = 0; s < KS; ++s) {
@@ -150,15 +156,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(&sm.s_full[g]);
       };
-      // O_g = P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major.
+      // O_g += P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major. O
+      // accumulates over the key tiles in TMEM.
       auto issue_pv = [&](int g, int j) {
-        const int s = j % KS;
+        const int s = j % KS, b = j % PB;
         const uint32_t tO = tmem + 256 * g + 128;
         for (int ks = 0; ks < kTile / 16; ++ks) {
-          mma_ss(tO, sw128_desc(smem_u32(sm.p[g][ks >> 2]) + (ks & 3) * 32, 16, 1024),
-                 sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024), idO, ks > 0);
+          mma_ss(tO, sw128_desc(smem_u32(sm.p[g][b][ks >> 2]) + (ks & 3) * 32, 16, 1024),
+                 sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024), idO,
+                 (j | ks) > 0);
         }
-        mma_commit(&sm.o_full[g]);
+        mma_commit(&sm.o_full[g][b]);
       };
       mbar_wait(&sm.q_ready, 0, abort_flag);
       mbar_wait(&sm.k_ready[0], 0, abort_flag);
@@ -180,10 +188,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             for (int g = 0; g < nact; ++g) issue_s(g, j + 1);
           }
         } else {
+          // S_g of tile j+1 goes ahead of P_g V of tile j (P is in shared
+          // memory, so S may overwrite the scores as soon as the softmax has
+          // published P): the group's next softmax overlaps this P V.
           for (int g = 0; g < nact; ++g) {
             mbar_wait(&sm.p_full[g], j & 1, abort_flag);
             tc_fence_after();
-            issue_pv(g, j);
             if (more) {
               if (g == 0) {
                 mbar_wait(&sm.k_ready[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag);
@@ -191,20 +201,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               }
               issue_s(g, j + 1);
             }
+            issue_pv(g, j);
           }
           mma_commit(&sm.kv_empty[j % KS]);
         }
       }
     }
-  } else if (warp < 4) {
+  } else if (warp < 4 || warp >= 12) {
     // ------------------------------------------------------------ rotation warps
-    // 64 threads; each warp rotates half of every tile, 16 rows at a time with
-    // the table values loaded before the tile's TMA wait.
-    const int rwp = warp - 2;
+    // Warps 2, 3, 12, 13; each rotates a quarter of every tile, 16 rows at a
+    // time with the table values loaded before the tile's TMA wait.
+    const int rwp = warp < 4 ? warp - 2 : warp - 10;
     auto rotate_tile = [&](uint8_t* tile, int tok0, uint64_t* full, uint32_t parity) {
 #pragma unroll 1
-      for (int blk = 0; blk < 4; ++blk) {
-        const int r0 = rwp * 64 + blk * 16;
+      for (int blk = 0; blk < 2; ++blk) {
+        const int r0 = rwp * 32 + blk * 16;
         RopeQ<NCH, 16> rope;
         load_rope_q<NCH, 16>(rope, r0, tok0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
         if (blk == 0) mbar_wait(full, parity, abort_flag);
@@ -214,13 +225,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int g = 0; g < nact; ++g)
       rotate_tile(&sm.q[g][0][0], (2 * pr + g) * kTile, &sm.q_full[g], 0);
     fence_proxy_async_smem();
-    named_bar(1, 64);
+    named_bar(1, 128);
     if (threadIdx.x == 64) mbar_arrive(&sm.q_ready);
     for (int j = 0; j < prm.nkv; ++j) {
       const int s = j % KS;
       rotate_tile(&sm.k[s][0][0], j * kTile, &sm.kv_full[s], (j / KS) & 1);
       fence_proxy_async_smem();
-      named_bar(1, 64);
+      named_bar(1, 128);
       if (threadIdx.x == 64) mbar_arrive(&sm.k_ready[s]);
     }
   } else {
@@ -238,9 +249,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tO = tmem + 256 * g + 128 + lane_off;
 
     if (g < nact) {
-      float o_acc[64 * NCH];
-#pragma unroll
-      for (int i = 0; i < 64 * NCH; ++i) o_acc[i] = 0.f;
       float m2 = -INFINITY, l = 0.f;
       const bool row_valid = qrow < N;
       // A warp whose 32 query rows are all padding skips the softmax math: its
@@ -252,10 +260,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int j = 0; j < prm.nkv; ++j) {
         const int kv0 = j * kTile;
         const int nvalid = min(kTile, N - kv0);
+        const int b = j % PB;
         mbar_wait(&sm.s_full[g], j & 1, abort_flag);
+        // P buffer b was last read by the P V of tile j - PB.
+        if (j >= PB) mbar_wait(&sm.o_full[g][b], ((j - PB) / PB) & 1, abort_flag);
         tc_fence_after();
         if (j == 0) FRSA_STAMP(4);
-        float alpha = 1.f;
         if (warp_active) {
           // pass 1: row max over the valid columns
           float mx = -INFINITY;
@@ -271,11 +281,38 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               for (int i = 0; i < 32; ++i)
                 if (h * 64 + u * 32 + i < nvalid) mx = fmaxf(mx, sv[u][i]);
           }
-          const float m_new = fmaxf(m2, mx * c2);
-          alpha = ex2(m2 - m_new);
-          // pass 2: P = exp2(S c2 - m), row sum, 16-bit P into this group's tile
+          // The exponent base m2 is raised only when a tile's maximum exceeds
+          // it by more than kFwdSlack (log2 units; P stays <= 2^kFwdSlack):
+          // then l and the O accumulated in TMEM so far are rescaled, after
+          // the previous P V has completed.
+          const bool up = mx * c2 > m2 + kFwdSlack;
+          if (__any_sync(0xffffffffu, up)) {
+            const float m_new = up ? mx * c2 : m2;
+            const float alpha = ex2(m2 - m_new);   // 0 on the first tile
+            l *= alpha;
+            if (j > 0) {
+              const int pj = j - 1;
+              mbar_wait(&sm.o_full[g][pj % PB], (pj / PB) & 1, abort_flag);
+              tc_fence_after();
+#pragma unroll
+              for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+                if (c16 * 16 < DP) {
+                  float ov[16];
+                  tmem_ld16(tO + c16 * 16, ov);
+                  tmem_wait_ld();
+                  uint32_t w[16];
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(ov[i] * alpha);
+                  tmem_st16(tO + c16 * 16, w);
+                }
+              }
+              tmem_wait_st();
+            }
+            m2 = m_new;
+          }
+          // pass 2: P = exp2(S c2 - m2), row sum, 16-bit P into buffer b
           float sum = 0.f;
-          const uint32_t pb0 = smem_u32(sm.p[g][0]);
+          const uint32_t pb0 = smem_u32(sm.p[g][b][0]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float sv[2][32];
@@ -288,13 +325,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               if (cbase + 32 <= nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                  sv[u][i] = ex2(fmaf(sv[u][i], c2, -m_new));
+                  sv[u][i] = ex2(fmaf(sv[u][i], c2, -m2));
                   sum += sv[u][i];
                 }
               } else if (cbase < nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                  sv[u][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[u][i], c2, -m_new)) : 0.f;
+                  sv[u][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[u][i], c2, -m2)) : 0.f;
                   sum += sv[u][i];
                 }
               } else {
@@ -312,42 +349,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               }
             }
           }
-          l = l * alpha + sum;
-          m2 = m_new;
+          l += sum;
         }
         fence_proxy_async_smem();
         tc_fence_before();
         named_bar(2 + g, 128);
         if (leader) mbar_arrive(&sm.p_full[g]);
         if (j == 0) FRSA_STAMP(5);
-
-        // O = O * alpha + P V
-        mbar_wait(&sm.o_full[g], j & 1, abort_flag);
-        tc_fence_after();
-        if (warp_active) {
-#pragma unroll
-          for (int c32 = 0; c32 < 2 * NCH; ++c32) {
-            if (c32 * 32 < DP) {
-              float ov[32];
-              tmem_ld32(tO + c32 * 32, ov);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                o_acc[c32 * 32 + i] = fmaf(o_acc[c32 * 32 + i], alpha, ov[i]);
-            }
-          }
-        }
-        tc_fence_before();
       }
       FRSA_STAMP(7);
 
-      // epilogue: lse = (m + log2 l) ln 2 and O / l, written through this
-      // group's P tile (free: the last P V has completed) as an f32 staging
-      // area, one 64-column block at a time, by warp-per-row coalesced stores.
+      // epilogue: lse = (m + log2 l) ln 2 and O / l, read from TMEM once the
+      // last P V has completed and written through this group's first P
+      // buffer (free) as an f32 staging area, one 64-column block at a time,
+      // by warp-per-row coalesced stores.
       if (row_valid)
         prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
+      {
+        const int lj = prm.nkv - 1;
+        mbar_wait(&sm.o_full[g][lj % PB], (lj / PB) & 1, abort_flag);
+        tc_fence_after();
+      }
       const float inv_l = warp_active ? 1.f / l : 0.f;
-      uint8_t* stage = &sm.p[g][0][0];
+      uint8_t* stage = &sm.p[g][0][0][0];
       T* o_head = reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D;
 #pragma unroll
       for (int blk = 0; blk < NCH; ++blk) {
@@ -355,8 +379,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int c16 = 0; c16 < 4; ++c16) {
             float v[16];
+            if (warp_active) {
+              tmem_ld16(tO + blk * 64 + c16 * 16, v);
+              tmem_wait_ld();
+            }
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = o_acc[blk * 64 + c16 * 16 + e] * inv_l;
+            for (int e = 0; e < 16; ++e) v[e] = warp_active ? v[e] * inv_l : 0.f;
             stage_write16<1>(stage, r, c16, v);
           }
           named_bar(2 + g, 128);
