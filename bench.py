@@ -311,7 +311,8 @@ def gpu_arm(args, world, rank, local):
                  "peak_source": psrc, "algorithmic_bytes_per_launch": bb,
                  "algorithmic_flops_per_launch": fb,
                  "tensor_frac": round(fb / (bwd_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)})
-    launches_per_step = 2 if (N <= 256 and D <= 64) else 3
+    # fwd + bwd; the general backward adds its Delta pass and dQ finalize.
+    launches_per_step = 2 if (N <= 256 and D <= 64) else 4
     mb = B * H * N * D * 2 / 1e6
     return {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,

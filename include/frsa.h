@@ -91,12 +91,13 @@ int frsa_fwd(const frsa_attn_args* args, void* stream);
  * Replaces the three launches of TritonAttention.backward
  * (_attn_bwd_preprocess fa_rope_full .py:1076-1082, _attn_bwd_dk_dv_rope
  * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136)
- * with one kernel (N <= 256 and D <= 64), or with a workspace clear, one
- * kernel and a dQ finalize pass otherwise. */
+ * with one kernel (N <= 256 and D <= 64), or otherwise with a workspace
+ * clear, a Delta pass, one kernel and a dQ finalize pass. */
 int frsa_bwd(const frsa_attn_args* args, void* stream);
 
 /* Bytes of fp32 workspace frsa_bwd needs for this shape (0 when the whole
- * head fits one CTA and dQ is reduced on chip). No reference counterpart:
+ * head fits one CTA and dQ is reduced on chip; else B*H*N*(D+1) floats: the
+ * dQ accumulator and the Delta rows). No reference counterpart:
  * the reference's dQ kernel (fa_rope_full .py:708-1009) recomputes instead. */
 size_t frsa_bwd_workspace_bytes(const frsa_attn_args* args);
 

@@ -127,7 +127,7 @@ def test_bwd_requires_gradients_and_workspace(lib):
     a = _args()
     assert lib.frsa_bwd(ctypes.byref(a), None) == 1              # no d_o / dq / dk / dv
     big = _args(N=257, n_pos=256, d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
-    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == 1 * 1 * 257 * 64 * 4
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == 1 * 1 * 257 * (64 + 1) * 4
     assert lib.frsa_bwd(ctypes.byref(big), None) == 9            # workspace missing
     small = _args(d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
     assert lib.frsa_bwd_workspace_bytes(ctypes.byref(small)) == 0

@@ -204,7 +204,8 @@ size_t frsa_bwd_workspace_bytes(const frsa_attn_args* a) {
   if (s.f32)   // Delta scratch of the float32 backward (unless args->delta is given)
     return frsa::tf32_bwd_supported(s) ? static_cast<size_t>(s.BH) * s.N * sizeof(float) : 0;
   if (!frsa::bwd_needs_workspace(s)) return 0;
-  return static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
+  // dQ accumulator (B*H*N*D floats), then Delta (B*H*N floats).
+  return static_cast<size_t>(s.BH) * s.N * (s.D + 1) * sizeof(float);
 }
 
 int frsa_fwd(const frsa_attn_args* a, void* stream) {
@@ -241,7 +242,7 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
     return FRSA_ERR_MISALIGNED;
   float* ws = nullptr;
   if (frsa::bwd_needs_workspace(s)) {
-    const size_t need = static_cast<size_t>(s.BH) * s.N * s.D * sizeof(float);
+    const size_t need = static_cast<size_t>(s.BH) * s.N * (s.D + 1) * sizeof(float);
     if (!a->workspace || a->workspace_bytes < need) return FRSA_ERR_WORKSPACE;
     if (!aligned16(a->workspace)) return FRSA_ERR_MISALIGNED;
     ws = static_cast<float*>(a->workspace);
@@ -257,6 +258,7 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
     return launch_error("frsa_bwd", cudaSuccess);
   const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, to, a->o, ws ? nullptr : tgrads, a->d_o, a->lse, a->delta,
                                          a->cosp, a->sinp, a->dq, a->dk, a->dv, ws,
+                                         ws ? (a->delta ? a->delta : ws + static_cast<size_t>(s.BH) * s.N * s.D) : nullptr,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);
 }

@@ -76,6 +76,9 @@ struct BwdParams {
   const float* lse;
   const void* o;
   float* delta_out;  // optional: receives Delta when non-null
+  // Optional (atomic mode): Delta of every row, computed by delta_rows_kernel
+  // before this kernel; when null the kernel forms Delta itself.
+  const float* delta_in = nullptr;
   void* dq;
   void* dk;
   void* dv;
@@ -320,6 +323,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       // O granules of this warp's query rows (quad layout), read before the
       // tile wait so the load overlaps it.
+      const bool dpre = !RESIDENT && prm.delta_in != nullptr;
+      if (dpre && g == 0)
+        sm.delta[qs_][r] = (q0_ + r) < N ? prm.delta_in[head_row0 + q0_ + r] : 0.f;
       const int rq = lane >> 3, gl = lane & 7;
       uint4 og[NCH][RW / 4];
 #pragma unroll
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int h = 0; h < NCH; ++h) {
           const int tok = q0_ + rw0 + 4 * k + rq, gg = gl + 8 * h;
-          og[h][k] = (tok < N && 8 * gg < D)
+          og[h][k] = (!dpre && tok < N && 8 * gg < D)
                          ? __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(prm.o) +
                                                                 (head_row0 + tok) * D) + gg)
                          : make_uint4(0u, 0u, 0u, 0u);
@@ -349,7 +355,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // the same granule of the (unrotated) dO tile; 8 lanes share a row.
       const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
 #pragma unroll
-      for (int k = 0; k < RW / 4; ++k) {
+      for (int k = 0; k < (dpre ? 0 : RW / 4); ++k) {
         float dl = 0.f;
 #pragma unroll
         for (int h = 0; h < NCH; ++h) {
@@ -621,6 +627,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // dQ = R^T dQ^ (dQ^ already scaled), one thread per 8 columns.
+// Delta = rowsum(dO * O) in f32 for every row of [B*H*N, D]: 8 lanes per
+// row, one 16-byte granule each per step (fa_rope_full .py:352-357).
+template <typename T>
+__global__ void delta_rows_kernel(const T* __restrict__ o, const T* __restrict__ d_o,
+                                  float* __restrict__ delta, long long rows, int D) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+  const int gl = threadIdx.x & 7;
+  float acc = 0.f;
+  if (row < rows) {
+    const uint4* orow = reinterpret_cast<const uint4*>(o + row * D);
+    const uint4* drow = reinterpret_cast<const uint4*>(d_o + row * D);
+    for (int gg = gl; 8 * gg < D; gg += 8) {
+      const uint4 a = __ldg(orow + gg), b = __ldg(drow + gg);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
+        acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+      }
+    }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (gl == 0 && row < rows) delta[row] = acc;
+}
+
 template <typename T>
 __global__ void dq_finalize_kernel(const float* __restrict__ acc, T* __restrict__ dq,
                                    const float* __restrict__ cosp, const float* __restrict__ sinp,
@@ -690,9 +724,8 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
                          const CUtensorMap& tm_o, const void* o,
                          const CUtensorMap* tm_grads, const void* d_o, const float* lse,
                          float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
-                         void* dv, float* dq_accum, cudaStream_t stream) {
+                         void* dv, float* dq_accum, float* delta_buf, cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
-  (void)d_o;
   BwdParams p;
   p.cosp = cosp;
   p.sinp = sinp;
@@ -719,6 +752,17 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   }
   e = cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
   if (e != cudaSuccess) return e;
+  if (delta_buf != nullptr) {
+    // Delta once per row here, instead of once per (key tile, query tile) in
+    // the main kernel (which would also re-read O for every key tile).
+    const long long threads_d = rows * 8;
+    delta_rows_kernel<T><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0, stream>>>(
+        static_cast<const T*>(o), static_cast<const T*>(d_o), delta_buf, rows, s.D);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    p.delta_in = delta_buf;
+    p.delta_out = nullptr;   // delta_buf is the caller's delta when one was given
+  }
   e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream)
                  : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream);
   if (e != cudaSuccess) return e;
@@ -737,12 +781,12 @@ cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUte
                        const void* o, const CUtensorMap* tm_grads,
                        const void* d_o, const float* lse, float* delta, const float* cosp,
                        const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
-                       cudaStream_t stream) {
+                       float* delta_buf, cudaStream_t stream) {
   if (s.bf16)
     return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse,
-                                       delta, cosp, sinp, dq, dk, dv, dq_accum, stream);
+                                       delta, cosp, sinp, dq, dk, dv, dq_accum, delta_buf, stream);
   return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse, delta, cosp,
-                              sinp, dq, dk, dv, dq_accum, stream);
+                              sinp, dq, dk, dv, dq_accum, delta_buf, stream);
 }
 
 }  // namespace frsa

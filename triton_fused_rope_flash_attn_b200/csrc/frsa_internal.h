@@ -74,6 +74,8 @@ cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUte
                        const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
                        const void* o, const CUtensorMap* tm_grads, const void* d_o, const float* lse,
                        float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
-                       void* dv, float* dq_accum, cudaStream_t stream);
+                       void* dv, float* dq_accum, float* delta_buf, cudaStream_t stream);
+// delta_buf (atomic mode, optional): B*H*N floats that receive Delta in a
+// pre-pass, which the main kernel then reads instead of forming it per tile.
 
 }  // namespace frsa
