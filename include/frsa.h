@@ -20,6 +20,8 @@
  *     default stream). Entry points never allocate device memory: scratch is
  *     passed in by the caller.
  *   - Return value 0 = launched; otherwise an FRSA_ERR_* code, nothing launched.
+ *     A CUDA error already pending on the calling thread (from the caller's
+ *     own earlier work) is reported as FRSA_ERR_LAUNCH and left pending.
  *   - Thread-safe; no global state except the device status word below.
  */
 #ifndef FRSA_H_
@@ -32,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FRSA_ABI_VERSION 1
+#define FRSA_ABI_VERSION 2
 
 enum frsa_dtype {
   FRSA_DTYPE_BF16 = 0,
@@ -91,28 +93,40 @@ int frsa_fwd(const frsa_attn_args* args, void* stream);
  * Replaces the three launches of TritonAttention.backward
  * (_attn_bwd_preprocess fa_rope_full .py:1076-1082, _attn_bwd_dk_dv_rope
  * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136)
- * with one kernel (N <= 256 and D <= 64), or otherwise with a workspace
- * clear, a Delta pass, one kernel and a dQ finalize pass. */
+ * with one persistent kernel (N <= 256 and D <= 64), or otherwise with a
+ * counter clear, a Delta pass and one persistent key-tile kernel whose dQ is
+ * reduced over key tiles in a fixed order. Results are bitwise reproducible
+ * from call to call in both cases. */
 int frsa_bwd(const frsa_attn_args* args, void* stream);
 
-/* Bytes of fp32 workspace frsa_bwd needs for this shape (0 when the whole
- * head fits one CTA and dQ is reduced on chip; else B*H*N*(D+1) floats: the
- * dQ accumulator and the Delta rows). No reference counterpart:
- * the reference's dQ kernel (fa_rope_full .py:708-1009) recomputes instead. */
+/* Bytes of workspace frsa_bwd needs for this shape: 0 when the whole head fits
+ * one CTA (N <= 256, D <= 64, 16-bit), else, for 16-bit compute, with
+ * T = ceil(N/128) key tiles and S = min(T, 8) partial-dQ slots,
+ *   S * B*H*N*D floats (partial dQ sums)
+ * + 4 * ((B*H*T*(1 + S) + 4) & ~3) bytes (arrival and slot counters, a claim ticket)
+ * + B*H*N floats (Delta rows), the last term only when args->delta is NULL;
+ * for F32 compute, B*H*N floats of Delta when args->delta is NULL.
+ * ABI version 2 (version 1 asked for B*H*N*(D+1) floats in every case).
+ * No reference counterpart: the reference's dQ kernel (fa_rope_full
+ * .py:708-1009) recomputes S and dP instead of reducing over key tiles. */
 size_t frsa_bwd_workspace_bytes(const frsa_attn_args* args);
 
 /* Backward pass that allocates nothing, for callers that cannot call
  * cudaMalloc: plugin hosts that only hand over input and output buffers,
  * runtimes whose device memory is fully carved up in advance, or loops that
  * must avoid cudaMalloc/cudaFree because those can synchronise the device.
- * Same arguments and results as frsa_bwd, but `workspace` is ignored: the f32
- * dQ accumulator lives in a fixed array inside the library (16 MiB per device,
- * kept until the process exits), so B*H*N*D must not exceed
- * frsa_bwd_noalloc_max_elements() (else FRSA_ERR_SCRATCH_LIMIT, nothing
- * launched). The first call on a device looks up that array's address (make
- * it before any stream capture). All calls on a device share the array: each
- * clears what it uses, and calls that run concurrently on the GPU race, so
- * order them on one stream. No counterpart in the reference. */
+ * Same arguments as frsa_bwd, but `workspace` is ignored and only 16-bit
+ * compute is accepted (F32 returns FRSA_ERR_UNSUPPORTED_DTYPE). Every shape
+ * runs the general key-tile kernel with the ordered dQ reduction, whose f32
+ * running sums and turn counters live in a fixed array inside the library
+ * (20 MiB per device, kept until the process exits), so B*H*N*D must not
+ * exceed frsa_bwd_noalloc_max_elements() (else FRSA_ERR_SCRATCH_LIMIT,
+ * nothing launched). Results agree with frsa_bwd's to rounding (bitwise for
+ * N > 256 or D > 64, where frsa_bwd runs the same kernel). The first call on a
+ * device looks up that array's address (make it before any stream capture).
+ * All calls on a device share the array: each clears the counters it uses,
+ * and calls that run concurrently on the GPU race, so order them on one
+ * stream. No counterpart in the reference. */
 int frsa_bwd_noalloc(const frsa_attn_args* args, void* stream);
 
 /* Largest B*H*N*D frsa_bwd_noalloc accepts (4 Mi elements). No counterpart in

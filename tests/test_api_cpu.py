@@ -70,7 +70,7 @@ def test_header_symbols_exported(lib):
     assert declared == set(_lib.EXPORTED_SYMBOLS)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.frsa_abi_version() == 1
+    assert lib.frsa_abi_version() == 2
 
 
 def test_strerror_covers_codes(lib):
@@ -118,6 +118,8 @@ def test_bwd_float32_contract(lib):
     assert lib.frsa_bwd(ctypes.byref(a), None) == 9          # workspace missing
     a.workspace, a.workspace_bytes = 0x4000, 197 * 4
     assert lib.frsa_bwd(ctypes.byref(a), None) == 8          # no sm_100 device here
+    a.delta = 0x5000
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(a)) == 0   # caller's delta: no scratch
     big = _args(io_dtype=_lib.FRSA_DTYPE_F32, compute_dtype=_lib.FRSA_DTYPE_F32, D=80, n_pos=196)
     big.d_o = big.dq = big.dk = big.dv = 0x3000
     assert lib.frsa_bwd(ctypes.byref(big), None) == 3        # D > 64: unsupported
@@ -127,8 +129,18 @@ def test_bwd_requires_gradients_and_workspace(lib):
     a = _args()
     assert lib.frsa_bwd(ctypes.byref(a), None) == 1              # no d_o / dq / dk / dv
     big = _args(N=257, n_pos=256, d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
-    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == 1 * 1 * 257 * (64 + 1) * 4
+    # ABI 2: S = min(T, 8) partial slots of B*H*N*D floats (T = 3 key tiles here),
+    # counters ((B*H*T*(1 + S) + 4) & ~3 int32) and Delta rows (B*H*N floats, only
+    # without a caller `delta`).
+    T = S = 3
+    counters = ((1 * 1 * T * (1 + S) + 4) & ~3) * 4
+    part = S * 257 * 64 * 4
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == part + counters + 257 * 4
+    big.delta = 0x2000
+    assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == part + counters
     assert lib.frsa_bwd(ctypes.byref(big), None) == 9            # workspace missing
+    big.workspace, big.workspace_bytes = 0x4000, part + counters
+    assert lib.frsa_bwd(ctypes.byref(big), None) == 8            # enough: no sm_100 device here
     small = _args(d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
     assert lib.frsa_bwd_workspace_bytes(ctypes.byref(small)) == 0
 
@@ -143,3 +155,15 @@ def test_table_shape_checked_by_wrapper():
         _check_tables(c[:, :16], c[:, :16], 197, 64, True, c.device)
     with pytest.raises(TypeError):
         _check_tables(c.double(), c.double(), 197, 64, True, c.device)
+
+
+def test_torch_extension_builds_binds_and_rejects_cpu_tensors():
+    """The PyTorch C++ extension (the product path's host side) loads, binds the
+    C ABI of libfrsa.so and refuses CPU tensors (there is no CPU path)."""
+    from triton_fused_rope_flash_attn_b200.attention import _ext, fused_rope_attention_fwd
+    ext = _ext()
+    assert hasattr(ext, "fwd") and hasattr(ext, "bwd")
+    q = torch.zeros(1, 1, 5, 64)
+    tab = torch.zeros(4, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused_rope_attention_fwd(q, q, q, tab, tab, True)

@@ -2,7 +2,8 @@
 many heads per CTA (ViT-B: 3072 heads on 148 SMs, ~21 per CTA), against an
 fp32 torch reference of the same operation on the GPU (PyTorch SDPA over
 Python-rotated q and k, the reference's described harness, README.md:123-136).
-The bar is the north-star tolerance: max abs <= 3e-2, mean abs <= 1e-3."""
+The bar is the north-star tolerance: max abs <= 3e-2, mean abs <= 1e-3 (see
+the ViT-H note below). Also the BASELINE plumbing config (fp32) exactly."""
 from __future__ import annotations
 
 import pytest
@@ -29,24 +30,107 @@ def _reference(q, k, v, do, cos, sin, has_cls):
     return o.detach(), q.grad, k.grad, v.grad
 
 
-@pytest.mark.parametrize("B,H,side,has_cls", [(256, 12, 14, True), (61, 7, 16, False),
-                                              (40, 16, 24, False)])
-def test_full_size_against_fp32_torch(B, H, side, has_cls):
-    from triton_fused_rope_flash_attn_b200 import CosSinTable, fused_rope_attention_bwd, \
-        fused_rope_attention_fwd
-    D = 64
+def _bf16_rounding_floor(ref):
+    """Mean abs error of rounding the exact result itself to bf16."""
+    return float((ref.bfloat16().float() - ref).abs().mean())
+
+
+# (B, H, H_img, has_cls, D, q/k/v amplitude): the four BASELINE attention
+# configs at their full batch, plus an odd head count at N = 256.
+FULL = {"vit_s": (512, 6, 14, True, 64, 1.0), "vit_b": (256, 12, 14, True, 64, 1.0),
+        "vit_l": (128, 16, 24, False, 64, 1.0), "vit_h": (64, 16, 37, True, 80, 2.0),
+        "odd_n256": (61, 7, 16, False, 64, 1.0)}
+
+
+def _torch_bf16(q, k, v, do, cos, sin, has_cls):
+    """The same operation in bf16 through torch's own fused SDPA (rotation in
+    fp32, rotated q/k rounded to bf16 like this repository's kernels do): a
+    yardstick for the error bf16 arithmetic alone costs at a given shape."""
+    import torch.nn.functional as F
+    N = q.shape[-2]
+    off = 1 if has_cls else 0
+    C = torch.ones(N, cos.shape[1], device=q.device)
+    S = torch.zeros(N, cos.shape[1], device=q.device)
+    C[off:], S[off:] = cos[: N - off], sin[: N - off]
+
+    def rot(x):
+        e, o = x[..., 0::2], x[..., 1::2]
+        return torch.stack((e * C - o * S, o * C + e * S), dim=-1).flatten(-2)
+
+    q, k, v = (t.float().requires_grad_(True) for t in (q, k, v))
+    o = F.scaled_dot_product_attention(rot(q).bfloat16(), rot(k).bfloat16(), v.bfloat16())
+    o.backward(do)
+    return o.detach().float(), q.grad, k.grad, v.grad
+
+
+@pytest.mark.parametrize("name", sorted(FULL))
+def test_full_size_against_fp32_torch(name):
+    """Through the public entry (sdpa_triton_fa_rope + autograd backward).
+
+    Bar: max abs <= 3e-2 and mean abs <= 1e-3 per tensor against the fp32
+    evaluation. ViT-H (q/k/v x2, D = 80) has logits of std ~4 and |O| up to
+    ~8, where a single bf16 rounding of P or O is worth ~1e-2 .. 3e-2 and the
+    exact O rounded to bf16 alone costs ~1e-3 mean: there the bounds are
+    widened to what bf16 arithmetic itself costs, measured on the same
+    inputs with torch's own bf16 fused SDPA (x1.5), and to twice the output
+    rounding floor; the relative mean error must stay <= 1e-2 everywhere.
+    Absolute, relative and yardstick errors are printed for every tensor.
+    """
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, _lib, sdpa_triton_fa_rope
+    B, H, side, has_cls, D, amp = FULL[name]
     N = side * side + (1 if has_cls else 0)
     g = torch.Generator(device="cuda").manual_seed(7)
-    q, k, v, do = (torch.randn(B, H, N, D, device="cuda", generator=g).bfloat16()
-                   for _ in range(4))
+    q, k, v, do = (torch.randn(B, H, N, D, device="cuda", generator=g) for _ in range(4))
+    q, k, v, do = ((q * amp).bfloat16(), (k * amp).bfloat16(), (v * amp).bfloat16(),
+                   do.bfloat16())
     cs = CosSinTable(100.0, side, D, device="cuda")
-    o, lse = fused_rope_attention_fwd(q, k, v, cs.COSP, cs.SINP, has_cls)
-    dq, dk, dv = fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = sdpa_triton_fa_rope(qd, kd, vd, cs, has_cls=has_cls, H_img=side)
+    o.backward(do)
     torch.cuda.synchronize()
-    from triton_fused_rope_flash_attn_b200 import _lib
     assert _lib.load().frsa_query_status() == 0
     refs = _reference(q, k, v, do, cs.COSP, cs.SINP, has_cls)
-    for name, got, ref in zip(("o", "dq", "dk", "dv"), (o, dq, dk, dv), refs):
+    yard = _torch_bf16(q, k, v, do, cs.COSP, cs.SINP, has_cls)
+    for tname, got, ref, ys in zip(("o", "dq", "dk", "dv"),
+                                   (o.detach(), qd.grad, kd.grad, vd.grad), refs, yard):
         d = (got.float() - ref).abs()
-        assert float(d.max()) <= 3e-2, (name, float(d.max()))
-        assert float(d.mean()) <= 1e-3, (name, float(d.mean()))
+        dy = (ys.float() - ref).abs()
+        mx, mean = float(d.max()), float(d.mean())
+        ymx, ymean = float(dy.max()), float(dy.mean())
+        rel = mean / float(ref.abs().mean())
+        floor = _bf16_rounding_floor(ref)
+        print(f"[{name} {tname}] max abs {mx:.3e} mean abs {mean:.3e} rel mean {rel:.3e} | "
+              f"torch bf16 SDPA max {ymx:.3e} mean {ymean:.3e} | bf16 floor {floor:.3e}")
+        assert mx <= max(3e-2, 1.5 * ymx), (tname, mx, ymx)
+        assert mean <= max(1e-3, 2.0 * floor, 1.5 * ymean), (tname, mean, ymean, floor)
+        assert rel <= 1e-2, (tname, rel)
+        if amp == 1.0:
+            assert mx <= 3e-2 and mean <= 1e-3, (tname, mx, mean)
+
+
+def test_plumbing_config_fp32():
+    """BASELINE's CPU-runnable plumbing config exactly: B=2, H=8, H_img=14,
+    has_cls (N=197), D=64, float32 inputs without autocast (the reference's
+    TF32 mode, fa_rope_full .py:65-73), q/k/v ~ N(0,1), base 100, upstream
+    gradient = ones (loss = o.sum()), against the float64 oracle."""
+    import numpy as np
+
+    from oracle import attn_bwd_np, attn_fwd_np
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, sdpa_triton_fa_rope
+    B, H, side, D = 2, 8, 14, 64
+    N = side * side + 1
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(B, H, N, D, generator=g) for _ in range(3))
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = sdpa_triton_fa_rope(qd, kd, vd, cs)
+    o.sum().backward()
+    assert o.dtype == torch.float32 and qd.grad.dtype == torch.float32
+    cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+    qn, kn, vn = (t.double().numpy() for t in (q, k, v))
+    o_ref, _ = attn_fwd_np(qn, kn, vn, cos, sin, True)
+    refs = (o_ref,) + attn_bwd_np(qn, kn, vn, np.ones_like(qn), cos, sin, True)
+    for tname, got, ref in zip(("o", "dq", "dk", "dv"), (o, qd.grad, kd.grad, vd.grad), refs):
+        d = np.abs(got.detach().double().cpu().numpy() - ref)
+        print(f"[plumbing fp32 {tname}] max abs {d.max():.3e} mean abs {d.mean():.3e}")
+        assert d.max() <= 3e-2 and d.mean() <= 1e-3, (tname, d.max(), d.mean())

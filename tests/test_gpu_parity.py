@@ -33,11 +33,13 @@ CASES = [
     (2, 4, 14, True, 64, 1.0, torch.bfloat16),    # N=197 (ViT-S/B)
     (2, 4, 14, True, 64, 1.0, torch.float16),     # N=197 fp16
     (1, 3, 16, False, 64, 1.0, torch.bfloat16),   # N=256
-    (1, 3, 16, True, 64, 1.0, torch.bfloat16),    # N=257 (atomic-dQ path)
+    (1, 3, 16, True, 64, 1.0, torch.bfloat16),    # N=257 (general path: ordered dQ)
+    (1, 3, 16, True, 64, 1.0, torch.float16),     # N=257 fp16 (Delta pre-pass for __half)
     (1, 2, 24, False, 64, 1.0, torch.bfloat16),   # N=576 (ViT-L)
     (1, 2, 14, True, 32, 1.0, torch.bfloat16),    # D=32
     (1, 2, 15, True, 48, 1.0, torch.bfloat16),    # D=48, N=226 (240 computed keys)
     (1, 2, 7, True, 80, 1.0, torch.bfloat16),     # D=80, N=50
+    (1, 2, 7, True, 80, 1.0, torch.float16),      # D=80 fp16 (general path)
     (1, 2, 14, True, 128, 1.0, torch.bfloat16),   # D=128
 ]
 
@@ -135,6 +137,34 @@ def test_deterministic_resident_path():
                                                         True))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,H,side,has_cls,D", [(4, 8, 24, False, 64),    # N=576: 5 key tiles
+                                                (1, 4, 37, True, 80),     # N=1370, D=80: 11
+                                                (2, 3, 16, True, 64)])    # N=257: 3 key tiles
+def test_deterministic_general_path(B, H, side, has_cls, D):
+    """N > 256 or D > 64: dQ is summed over key tiles in a fixed order, so
+    repeated runs are bitwise identical even though CTAs claim work in
+    whatever order they reach the ticket counter. A differently shaped call in
+    between changes the timing of the next run."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, fused_rope_attention_bwd, \
+        fused_rope_attention_fwd
+    N = side * side + int(has_cls)
+    q, k, v, do = (t.cuda().bfloat16() for t in seeded_inputs(B, H, N, D, seed=5))
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    o, lse = fused_rope_attention_fwd(q, k, v, cs.COSP, cs.SINP, has_cls)
+    first = fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls)
+    for rep in range(3):
+        xs = torch.randn(3 + rep, 2, N, D, device="cuda").bfloat16()
+        fused_rope_attention_bwd(xs, xs, xs, *fused_rope_attention_fwd(xs, xs, xs, cs.COSP,
+                                                                       cs.SINP, has_cls),
+                                 xs, cs.COSP, cs.SINP, has_cls)
+        again = fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls)
+        for name, a, b in zip(("dq", "dk", "dv"), first, again):
+            assert torch.equal(a, b), (rep, name)
+    from triton_fused_rope_flash_attn_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.load().frsa_query_status() == 0
 
 
 @pytest.mark.parametrize("side,has_cls", [(14, True), (24, False)])

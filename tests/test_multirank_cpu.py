@@ -2,8 +2,9 @@
 
 Covers what the multi-GPU bench relies on besides the kernels: rank/world
 from the environment, the barrier, and the max-over-ranks of the step time
-(the slowest rank defines the job's time), and that the whole-job value sums
-the work of all ranks over that time.
+(the slowest rank defines the job's time), the per-rank breakdown every rank
+gathers, and that the whole-job value sums the work of all ranks over that
+time.
 """
 from __future__ import annotations
 
@@ -29,7 +30,8 @@ def _worker(rank, world, port, out):
     bench.barrier(w)
     step_ms = 1.0 + rank            # rank 1 is the slow one
     worst = bench.max_over_ranks(step_ms, w, "cpu")
-    out[rank] = worst
+    rows = bench.gather_rows([step_ms, 10.0 * rank], w, "cpu")   # per-rank breakdown
+    out[rank] = (worst, rows)
     dist.destroy_process_group()
 
 
@@ -39,4 +41,5 @@ def test_two_gloo_ranks_max_over_ranks():
     with mp.Manager() as m:
         out = m.dict()
         mp.spawn(_worker, args=(world, port, out), nprocs=world, join=True)
-        assert dict(out) == {0: 2.0, 1: 2.0}
+        expect = (2.0, [[1.0, 0.0], [2.0, 10.0]])
+        assert dict(out) == {0: expect, 1: expect}

@@ -7,7 +7,8 @@ synchronise the device). It keeps its f32 dQ accumulator in a fixed array
 inside the library instead of a caller-provided workspace. This file calls it
 through the C ABI, twice in a row (the array keeps the previous call's
 contents, so the second call checks that each call clears what it uses), and
-compares dQ, dK, dV with frsa_bwd under the parity bar of the other GPU tests.
+compares dQ, dK, dV with frsa_bwd and with the float64 oracle under the parity
+bar of the other GPU tests.
 
 Named so pytest collects it last; it also passes when run alone.
 """
@@ -19,6 +20,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import attn_bwd_np
 from tests.helpers import MAX_ABS_TOL, MEAN_ABS_TOL, err_stats, seeded_inputs
 
 pytestmark = pytest.mark.gpu
@@ -36,16 +38,18 @@ def _call_noalloc(q, k, v, o, lse, do, cosp, sinp, has_cls):
     return dq, dk, dv
 
 
-@pytest.mark.parametrize("B,H,side,has_cls,D", [(2, 4, 14, True, 64),    # regular path: on-chip dQ
-                                                (1, 3, 16, True, 64),    # regular path: workspace
-                                                (1, 2, 7, True, 80)])
-def test_noalloc_matches_regular_backward_twice(B, H, side, has_cls, D):
+@pytest.mark.parametrize("B,H,side,has_cls,D,dtype", [
+    (2, 4, 14, True, 64, torch.bfloat16),    # regular path: on-chip dQ
+    (1, 3, 16, True, 64, torch.bfloat16),    # regular path: workspace
+    (1, 2, 7, True, 80, torch.bfloat16),
+    (1, 3, 16, True, 64, torch.float16)])
+def test_noalloc_matches_regular_backward_twice(B, H, side, has_cls, D, dtype):
     from triton_fused_rope_flash_attn_b200 import (CosSinTable, _lib, fused_rope_attention_bwd,
                                                    fused_rope_attention_fwd)
     N = side * side + int(has_cls)
     cs = CosSinTable(100.0, side, D, device="cuda")
     for call in range(2):
-        q, k, v, do = (t.cuda().bfloat16() for t in seeded_inputs(B, H, N, D, seed=11 + call))
+        q, k, v, do = (t.cuda().to(dtype) for t in seeded_inputs(B, H, N, D, seed=11 + call))
         o, lse = fused_rope_attention_fwd(q, k, v, cs.COSP, cs.SINP, has_cls)
         ref = fused_rope_attention_bwd(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls)
         got = _call_noalloc(q, k, v, o, lse, do, cs.COSP, cs.SINP, has_cls)
@@ -56,6 +60,25 @@ def test_noalloc_matches_regular_backward_twice(B, H, side, has_cls, D):
             assert np.isfinite(gn).all(), name
             mx, mean = err_stats(gn, rn)
             assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (call, name, mx, mean)
+        # and against the float64 oracle on the same quantised inputs
+        cos, sin = cs.COSP.cpu().numpy(), cs.SINP.cpu().numpy()
+        exact = attn_bwd_np(*(t.double().cpu().numpy() for t in (q, k, v, do)), cos, sin,
+                            has_cls)
+        for name, g, r in zip(("dq", "dk", "dv"), got, exact):
+            mx, mean = err_stats(g.double().cpu().numpy(), r)
+            assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, ("oracle", call, name, mx, mean)
+
+
+def test_noalloc_rejects_float32():
+    """Only 16-bit compute: float32 tensors are refused before anything launches."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, _lib
+    from triton_fused_rope_flash_attn_b200.attention import _make_args
+    cs = CosSinTable(100.0, 4, 64, device="cuda")
+    q = torch.zeros(1, 1, 17, 64, device="cuda")
+    lse = torch.zeros(1, 1, 17, device="cuda")
+    a = _make_args(q, q, q, cs.COSP, cs.SINP, True, torch.float32, o=q, lse=lse, d_o=q, dq=q,
+                   dk=q, dv=q)
+    assert _lib.load().frsa_bwd_noalloc(ctypes.byref(a), None) == 4    # UNSUPPORTED_DTYPE
 
 
 def test_noalloc_rejects_oversize():

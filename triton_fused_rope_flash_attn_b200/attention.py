@@ -54,10 +54,6 @@ def _make_args(q, k, v, cosp, sinp, has_cls, comp, o=None, lse=None, d_o=None, d
     return a
 
 
-def _stream_handle(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
-
-
 def _check_tables(cosp, sinp, N, D, has_cls, device):
     if cosp.dtype != torch.float32 or sinp.dtype != torch.float32:
         raise TypeError("COSP/SINP must be float32")
@@ -71,20 +67,36 @@ def _check_tables(cosp, sinp, N, D, has_cls, device):
         raise ValueError("RoPE tables must be on the same device as Q")
 
 
+_EXT = None
+
+
+def _ext():
+    """The PyTorch C++ extension (``csrc/frsa_torch.cpp``), bound to the loaded C ABI.
+
+    Built in-tree on first use if missing; there is no fallback path.
+    """
+    global _EXT
+    if _EXT is None:
+        import ctypes
+        from .build import build_torch_ext
+        lib = _lib.load()
+        if lib.frsa_abi_version() != 2:
+            raise RuntimeError(f"libfrsa.so ABI version {lib.frsa_abi_version()}, expected 2")
+        ext = build_torch_ext()
+        addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value  # noqa: E731
+        ext.bind(addr(lib.frsa_fwd), addr(lib.frsa_bwd), addr(lib.frsa_bwd_workspace_bytes))
+        _EXT = ext
+    return _EXT
+
+
 def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True, scale=None):
-    """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]`` bf16/f16.
+    """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]``, all bf16, f16 or f32.
 
     Returns ``(o, lse)`` with ``lse`` float32 ``[B, H, N]`` (natural log).
     ``scale`` multiplies the logits (default ``1/sqrt(D)``).
     """
-    comp = q.dtype
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    cosp, sinp = cosp.contiguous(), sinp.contiguous()
-    B, H, N, D = q.shape
-    o = torch.empty_like(q)
-    lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, scale=scale)
-    _lib.check(_lib.load().frsa_fwd(a, _stream_handle(q.device)), "frsa_fwd")
+    o, lse, rc = _ext().fwd(q, k, v, cosp, sinp, bool(has_cls), -1.0 if scale is None else scale)
+    _lib.check(rc, "frsa_fwd")
     return o, lse
 
 
@@ -94,21 +106,9 @@ def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = T
 
     ``delta_out`` (optional float32 ``[B, H, N]``) receives ``rowsum(dO * O)``.
     """
-    comp = q.dtype
-    q, k, v, o, d_o = (t.contiguous() for t in (q, k, v, o, d_o))
-    cosp, sinp = cosp.contiguous(), sinp.contiguous()
-    B, H, N, D = q.shape
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    a = _make_args(q, k, v, cosp, sinp, has_cls, comp, o=o, lse=lse, d_o=d_o, dq=dq, dk=dk,
-                   dv=dv, delta=delta_out, scale=scale)
-    lib = _lib.load()
-    ws_bytes = lib.frsa_bwd_workspace_bytes(a)
-    ws = None
-    if ws_bytes:
-        ws = torch.empty(ws_bytes // 4, device=q.device, dtype=torch.float32)
-        a.workspace = ws.data_ptr()
-        a.workspace_bytes = ws_bytes
-    _lib.check(lib.frsa_bwd(a, _stream_handle(q.device)), "frsa_bwd")
+    dq, dk, dv, rc = _ext().bwd(q, k, v, o, lse, d_o, cosp, sinp, bool(has_cls), delta_out,
+                                -1.0 if scale is None else scale)
+    _lib.check(rc, "frsa_bwd")
     return dq, dk, dv
 
 

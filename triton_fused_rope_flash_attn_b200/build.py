@@ -1,10 +1,13 @@
-"""Build the sm_100a C-ABI library ``_lib/libfrsa.so`` in-tree with nvcc.
+"""Build the sm_100a C-ABI library ``_lib/libfrsa.so`` and the PyTorch C++
+extension over it (``_lib/torch_ext/frsa_torch_ext*.so``), both in-tree.
 
     python -m triton_fused_rope_flash_attn_b200.build [--force]
 
 The library is one translation unit (``csrc/frsa_api.cu`` includes the kernel
 files). It links only the CUDA runtime; the TMA tensor-map encoder is fetched
-from the driver at run time.
+from the driver at run time. The extension (``csrc/frsa_torch.cpp``) is the
+host side of the product path; it binds the C-ABI entry points of the loaded
+library at run time, so it does not link against it.
 """
 from __future__ import annotations
 
@@ -69,5 +72,23 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
+
+
+
+TORCH_EXT_NAME = "frsa_torch_ext"
+TORCH_EXT_DIR = os.path.join(LIB_DIR, "torch_ext")
+TORCH_EXT_SRC = os.path.join(CSRC, "frsa_torch.cpp")
+
+
+def build_torch_ext(verbose: bool = False):
+    """Compile (or load the up-to-date build of) the PyTorch extension; returns the module."""
+    import torch.utils.cpp_extension as ce
+    os.makedirs(TORCH_EXT_DIR, exist_ok=True)
+    return ce.load(name=TORCH_EXT_NAME, sources=[TORCH_EXT_SRC], extra_include_paths=[INCLUDE],
+                   extra_cflags=["-O3", "-std=c++17"], build_directory=TORCH_EXT_DIR,
+                   with_cuda=True, verbose=verbose)
+
+
 if __name__ == "__main__":
     print(build_library(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_torch_ext(verbose="-v" in sys.argv).__file__)

@@ -19,6 +19,40 @@
 #include "frsa_tf32.cu"
 #include "frsa_qkv.cu"
 
+namespace frsa {
+
+int device_sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+cudaError_t set_max_dynamic_smem_once(const void* kernel, size_t bytes) {
+  // (kernel, device) pairs already configured; the library has ~20 kernels.
+  struct Entry { const void* k; int dev; size_t bytes; };
+  static Entry done[256];
+  static int ndone = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < ndone; ++i)
+    if (done[i].k == kernel && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes));
+  if (e == cudaSuccess && ndone < 256) done[ndone++] = Entry{kernel, dev, bytes};
+  return e;
+}
+
+}  // namespace frsa
+
 namespace {
 
 using frsa::kTile;
@@ -57,6 +91,8 @@ bool device_is_sm100() {
 }
 
 thread_local int g_last_encode_result = 0;
+// Detail of the last FRSA_ERR_LAUNCH on this host thread.
+thread_local char g_last_detail[256] = "";
 
 // 3-D map over a contiguous [BH, N, D] 16-bit tensor: dims {D, N, BH}, box
 // {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor. For float32
@@ -102,8 +138,6 @@ bool encode_map_2d(CUtensorMap* m, const void* base, long long rows, long long c
   return r == CUDA_SUCCESS;
 }
 
-// Detail of the last FRSA_ERR_LAUNCH on this host thread.
-thread_local char g_last_detail[256] = "";
 
 int launch_error(const char* where, cudaError_t e) {
   if (e == cudaSuccess)
@@ -116,6 +150,27 @@ int launch_error(const char* where, cudaError_t e) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// f32 map {D, N, nslot * BH} over the general backward's partial-dQ slots,
+// box {32, 128, 1}, 128-byte swizzle.
+bool encode_part_map(CUtensorMap* m, const float* part, const frsa::LaunchShape& s, int nslot) {
+  frsa::LaunchShape p = s;
+  p.f32 = true;
+  p.BH = s.BH * nslot;
+  return encode_map(m, part, p);
+}
+
+// A CUDA error already pending on this host thread (left by the caller's own
+// earlier work) is reported, not cleared: nothing is launched, the error stays
+// pending for its owner, and the detail string names it.
+int pending_error(const char* where) {
+  const cudaError_t e = cudaPeekAtLastError();
+  if (e == cudaSuccess) return FRSA_OK;
+  snprintf(g_last_detail, sizeof(g_last_detail),
+           "%s: a CUDA error was already pending before this call: %s (%d)", where,
+           cudaGetErrorString(e), static_cast<int>(e));
+  return FRSA_ERR_LAUNCH;
+}
 
 int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   if (!a) return FRSA_ERR_NULL_ARG;
@@ -144,6 +199,16 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   return FRSA_OK;
 }
 
+// Workspace of the general 16-bit backward: the f32 partial dQ sums (S slots
+// of BH*N*D floats, S = min(key tiles, 8)), the counters and claim ticket,
+// and, unless the caller passes `delta`, the Delta rows (BH*N floats).
+size_t general_bwd_workspace_bytes(const frsa::LaunchShape& s, bool caller_delta) {
+  const size_t rows = static_cast<size_t>(s.BH) * s.N;
+  const int S = frsa::bwd_slots(s);
+  return S * rows * s.D * sizeof(float) + frsa::bwd_counter_ints(s, S) * sizeof(int) +
+         (caller_delta ? 0 : rows * sizeof(float));
+}
+
 // float32 backward (TF32 tensor cores), D <= 64.
 int bwd_f32(const frsa_attn_args* a, const frsa::LaunchShape& s, void* stream) {
   if (!frsa::tf32_bwd_supported(s)) return FRSA_ERR_UNSUPPORTED_D;
@@ -159,7 +224,7 @@ int bwd_f32(const frsa_attn_args* a, const frsa::LaunchShape& s, void* stream) {
   }
   if (!aligned16(delta)) return FRSA_ERR_MISALIGNED;
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
-  (void)cudaGetLastError();
+  if (const int rc = pending_error("frsa_bwd"); rc != FRSA_OK) return rc;
   CUtensorMap maps[7];   // q16, q32, k16, k32, v16, do16, do32
   if (!encode_map(&maps[0], a->q, s) || !encode_map(&maps[1], a->q, s, true) ||
       !encode_map(&maps[2], a->k, s) || !encode_map(&maps[3], a->k, s, true) ||
@@ -202,10 +267,10 @@ size_t frsa_bwd_workspace_bytes(const frsa_attn_args* a) {
   frsa::LaunchShape s;
   if (validate_common(a, &s) != FRSA_OK) return 0;
   if (s.f32)   // Delta scratch of the float32 backward (unless args->delta is given)
-    return frsa::tf32_bwd_supported(s) ? static_cast<size_t>(s.BH) * s.N * sizeof(float) : 0;
+    return (frsa::tf32_bwd_supported(s) && a->delta == nullptr)
+               ? static_cast<size_t>(s.BH) * s.N * sizeof(float) : 0;
   if (!frsa::bwd_needs_workspace(s)) return 0;
-  // dQ accumulator (B*H*N*D floats), then Delta (B*H*N floats).
-  return static_cast<size_t>(s.BH) * s.N * (s.D + 1) * sizeof(float);
+  return general_bwd_workspace_bytes(s, a->delta != nullptr);
 }
 
 int frsa_fwd(const frsa_attn_args* a, void* stream) {
@@ -215,9 +280,7 @@ int frsa_fwd(const frsa_attn_args* a, void* stream) {
   if (!a->o || !a->lse) return FRSA_ERR_NULL_ARG;
   if (!aligned16(a->o) || !aligned16(a->lse)) return FRSA_ERR_MISALIGNED;
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
-  // A non-sticky error left on this host thread by an earlier runtime call
-  // (e.g. cudaErrorNotReady from an event poll) must not be blamed on our launch.
-  (void)cudaGetLastError();
+  if ((rc = pending_error("frsa_fwd")) != FRSA_OK) return rc;
   CUtensorMap tq, tk, tv, to;
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) ||
       !encode_map(&tv, a->v, s, /*atom32=*/s.f32) || !encode_map(&to, a->o, s))
@@ -240,26 +303,42 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
   if (!aligned16(a->o) || !aligned16(a->d_o) || !aligned16(a->dq) || !aligned16(a->dk) ||
       !aligned16(a->dv) || !aligned16(a->lse))
     return FRSA_ERR_MISALIGNED;
-  float* ws = nullptr;
-  if (frsa::bwd_needs_workspace(s)) {
-    const size_t need = static_cast<size_t>(s.BH) * s.N * (s.D + 1) * sizeof(float);
-    if (!a->workspace || a->workspace_bytes < need) return FRSA_ERR_WORKSPACE;
+  const bool general = frsa::bwd_needs_workspace(s);
+  if (general) {
+    if (!a->workspace || a->workspace_bytes < general_bwd_workspace_bytes(s, a->delta != nullptr))
+      return FRSA_ERR_WORKSPACE;
     if (!aligned16(a->workspace)) return FRSA_ERR_MISALIGNED;
-    ws = static_cast<float*>(a->workspace);
   }
+  if (a->delta && !aligned16(a->delta)) return FRSA_ERR_MISALIGNED;
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
-  (void)cudaGetLastError();  // see frsa_fwd
+  if ((rc = pending_error("frsa_bwd")) != FRSA_OK) return rc;
   CUtensorMap tq, tk, tv, tdo, to, tgrads[3];
   if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
       !encode_map(&tdo, a->d_o, s) || !encode_map(&to, a->o, s))
     return launch_error("frsa_bwd", cudaSuccess);
-  if (ws == nullptr && (!encode_map(&tgrads[0], a->dq, s) || !encode_map(&tgrads[1], a->dk, s) ||
-                        !encode_map(&tgrads[2], a->dv, s)))
-    return launch_error("frsa_bwd", cudaSuccess);
-  const cudaError_t e = frsa::launch_bwd(s, tq, tk, tv, tdo, to, a->o, ws ? nullptr : tgrads, a->d_o, a->lse, a->delta,
-                                         a->cosp, a->sinp, a->dq, a->dk, a->dv, ws,
-                                         ws ? (a->delta ? a->delta : ws + static_cast<size_t>(s.BH) * s.N * s.D) : nullptr,
-                                         static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (!general) {
+    if (!encode_map(&tgrads[0], a->dq, s) || !encode_map(&tgrads[1], a->dk, s) ||
+        !encode_map(&tgrads[2], a->dv, s))
+      return launch_error("frsa_bwd", cudaSuccess);
+    e = frsa::launch_bwd_small(s, tq, tk, tv, tdo, to, tgrads, a->o, a->lse, a->delta, a->cosp,
+                               a->sinp, a->dq, a->dk, a->dv, st);
+  } else {
+    const size_t rows = static_cast<size_t>(s.BH) * s.N;
+    const int S = frsa::bwd_slots(s);
+    float* part = static_cast<float*>(a->workspace);
+    int* counters = reinterpret_cast<int*>(part + S * rows * s.D);
+    float* delta_rows = a->delta ? a->delta
+                                 : reinterpret_cast<float*>(counters + frsa::bwd_counter_ints(s, S));
+    CUtensorMap tpart;
+    if (!encode_map(&tgrads[1], a->dk, s) || !encode_map(&tgrads[2], a->dv, s) ||
+        !encode_part_map(&tpart, part, s, S))
+      return launch_error("frsa_bwd", cudaSuccess);
+    e = frsa::launch_bwd_ordered(s, tq, tk, tv, tdo, to, tgrads[1], tgrads[2], tpart, a->o, a->d_o,
+                                 a->lse, a->delta, a->cosp, a->sinp, a->dq, a->dk, a->dv, part, S,
+                                 counters, delta_rows, st);
+  }
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);
 }
 
@@ -281,7 +360,7 @@ int frsa_qkv_rope(const frsa_qkv_args* a, void* stream) {
       !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) || !aligned16(a->sinp))
     return FRSA_ERR_MISALIGNED;
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
-  (void)cudaGetLastError();
+  if (const int rc = pending_error("frsa_qkv_rope"); rc != FRSA_OK) return rc;
   const bool bf16 = a->dtype == FRSA_DTYPE_BF16;
   CUtensorMap tx, tw;
   if (!encode_map_2d(&tx, a->x, M, a->C, bf16) || !encode_map_2d(&tw, a->w, 3 * a->C, a->C, bf16))

@@ -1,37 +1,58 @@
-// Backward kernels: dQ, dK, dV of softmax(R(Q) R(K)^T * scale) V.
+// Backward kernels: dQ, dK, dV of softmax(R(Q) R(K)^T * scale) V for the shapes
+// the persistent single-head kernel (frsa_bwd_small.cu) does not cover
+// (N > 256 or D > 64).
 //
 // Restates _attn_bwd_preprocess, _attn_bwd_dk_dv_rope and _attn_bwd_dq_rope
 // (fa_rope_full .py:325-357, 374-691, 708-1009) as:
 //
-//   bwd_kernel    key-major tcgen05 kernel. When a query tile arrives the row
-//                 warpgroup first forms Delta = rowsum(dO * O) in f32 from the
-//                 dO tile in shared memory and the O row in global memory
-//                 (fa_rope_full .py:352-357), so no separate preprocess launch. A CTA owns 128-key tiles of one
-//                 (batch*head) and loops over all 128-query tiles:
+//   delta_rows    Delta = rowsum(dO * O) once per row (fa_rope_full .py:352-357).
+//   bwd_kernel    persistent key-major tcgen05 kernel. A work unit is one
+//                 (batch*head, 128-key tile); CTAs claim units in increasing
+//                 order from a ticket counter and walk every 128-query tile:
 //                   S^T  = K^ Q^T            (TMEM, f32)
 //                   dP^T = V dO^T            (TMEM, f32)
 //                   P    = exp2(S^T c2 - lse2_q),  dS = P (dP - Delta_q)  (registers)
 //                   dV  += P dO,  dK^ += dS Q^  (TMEM accumulators)
-//                   dQ^ += dS^T K^           (TMEM)
+//                   dQ^_j = dS^T K^          (TMEM, this key tile's share)
 //                 P and dS are written once to shared memory as [key][query]
 //                 tiles; the dQ product reads the same dS tile query-major.
-//                 "Resident" mode (N <= 256, D <= 64): one CTA per head walks
-//                 every key tile and keeps both dQ^ tiles in TMEM, so dQ is
-//                 finished on chip with no atomics (deterministic).
-//                 "Atomic" mode (any N): one CTA per (head, key tile); each
-//                 dQ^ partial is scaled and added into an f32 workspace.
-//   dq_finalize   (atomic mode) dQ = R^T dQ^ rounded to the I/O type.
+//
+// dQ is reduced over key tiles in a fixed order, so the result is bitwise
+// reproducible (the reference's dQ kernel is deterministic too: one program
+// per query tile, fa_rope_full .py:708-1009). Key tile j of a head writes its
+// scaled dQ^ share of query tile i into partial slot s = j % S of the
+// workspace (S = nslot; when key tiles share a slot, j >= S first waits for
+// its predecessor j - S in that slot and adds to it, so each slot holds the
+// in-order sum of its key tiles). It then counts itself in on a per-(head,
+// query tile) arrival counter; the CTA that arrives last sums the S slots in
+// slot order, un-rotates with R^T (fa_rope_full .py:974-993) and writes dQ in
+// the I/O type, then discards the slots' L2 lines (they are dead; this saves
+// their write-back to DRAM). No CTA waits for another unless slots are
+// shared, and then only for a unit claimed S units earlier. Units are claimed
+// in order, so a unit waited for is always held by a running CTA; every wait
+// is bounded.
 //
 // Compared with the reference, S and dP are computed once per (key tile,
 // query tile) pair instead of twice, and no separate dQ pass recomputes them.
 //
-// Warp roles in bwd_kernel: warp 0 TMA producer, warp 1 TMEM allocator + MMA
-// issuer, warps 2..5 the row warpgroup (thread = key row of the tile; for dQ
-// read-back thread = query row).
+// Warp roles in bwd_kernel: warp 0 TMA producer (and unit claims), warp 1
+// TMEM allocator + MMA issuer, warps 4..11 two row warpgroups (thread = key
+// row of the tile; for dQ read-back thread = query row).
 //
-// TMEM columns: [0,128) S^T, [128,256) dP^T (atomic mode: reused for the dQ^
-// partial), [256, 256+DP) dV, [256+DP, 256+2DP) dK^, resident mode:
-// [384 + 64 i, 448 + 64 i) dQ^ of query tile i.
+// TMEM columns: [0,128) S^T, [128,256) dP^T, [256, 256+DP) dV,
+// [256+DP, 256+2DP) dK^, [256+2DP, 256+3DP) the dQ^ share when that fits in
+// 512 columns (D <= 80), else the dQ^ share reuses the dP^T columns.
+//
+// Pipelining (per CTA). An iteration is one (key tile, query tile) pair; the
+// iterations of consecutive units form one sequence. For D <= 64 (two query
+// stages) the MMA warp issues S^T/dP^T of iteration t + 1 as soon as the row
+// warps have loaded iteration t's S^T/dP^T into registers, before issuing the
+// gradient products of t, and the row warps drain iteration t - 1's dQ^
+// share (and, at a unit's end, its dV and dK^) while the tensor core runs the
+// products of t: the exponentials of one iteration overlap the products of
+// the neighbouring ones. With one query stage (D > 64) the next query tile
+// can only load once t's products are done, so t's results are drained and
+// the next tile prepared right after them.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
@@ -50,6 +71,12 @@ constexpr int kBwdThreads = 128 + kComputeThreads;    // + warpgroup 0: producer
 constexpr uint32_t kRegsCtl = 96, kRegsCompute = 200;
 constexpr int kRowsPerWarp = kTile / (kComputeThreads / 32);  // 16
 constexpr uint32_t kTmemColsBwd = 512;
+constexpr int kUnitRing = 4;   // claimed units published by the producer
+}  // namespace
+// Partial dQ slots of the general backward (frsa_bwd): key tiles j and j + 8
+// share a slot, in order.
+constexpr int kMaxDqSlots = 8;
+namespace {
 
 template <int NCH>
 struct BwdSmem {
@@ -61,11 +88,18 @@ struct BwdSmem {
   uint8_t dO[QS][NCH][kChunkBytes];
   uint8_t p[2][kChunkBytes];   // P  [128 key][128 query], two 64-column chunks
   uint8_t ds[2][kChunkBytes];  // dS [128 key][128 query]
+  // Store staging for one CTA-wide result tile (D <= 64: the dV and dK^
+  // tiles, then the f32 dQ^ share); with one query stage the P/dS tiles,
+  // which are idle while results drain, serve instead.
+  uint8_t stage[(NCH == 1) ? 2 : 1][kChunkBytes];
   float lse2[QS][kTile];       // lse * log2(e) of the query tile
   float delta[QS][kTile];
   uint64_t kv_full[KVS], kv_empty[KVS];
   uint64_t q_full[QS], q_empty[QS];
-  uint64_t kq_ready, st_full, ds_full, mm_done, tm_free, acc_free, dq_free;
+  uint64_t kq_ready, st_full, st_free, ds_full, mm_done, dq_free, acc_free;
+  uint64_t unit_full[kUnitRing], unit_empty[kUnitRing];
+  int unit[kUnitRing];
+  int last_arrival;            // broadcast: this CTA completes the dQ of the query tile
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -75,28 +109,33 @@ struct BwdParams {
   const float* sinp;
   const float* lse;
   const void* o;
-  float* delta_out;  // optional: receives Delta when non-null
-  // Optional (atomic mode): Delta of every row, computed by delta_rows_kernel
-  // before this kernel; when null the kernel forms Delta itself.
+  float* delta_out;  // optional: receives Delta when non-null (in-kernel Delta only)
+  // Optional: Delta of every row, computed by delta_rows_kernel before this
+  // kernel; when null the kernel forms Delta itself.
   const float* delta_in = nullptr;
   void* dq;
   void* dk;
   void* dv;
-  float* dq_accum;
+  float* dq_part;    // f32 [nslot][BH, N, D] partial dQ^ sums (no initial value needed)
+  int* arrive;       // [BH * nqt] arrival counters, zero at launch
+  int* turns;        // [BH * nqt * nslot] slot turn counters, zero at launch
+  int* ticket;       // unit claim counter, zero at launch
+  int nslot;         // partial slots S (1 .. nkv)
   int BH, N, D, nqt, nkv, has_cls;
   float c2;     // scale * log2(e)
   float scale;
 };
 
-template <typename T, int NCH, bool RESIDENT>
+template <typename T, int NCH>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-               const __grid_constant__ CUtensorMap tm_o, const BwdParams prm) {
+               const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_dk,
+               const __grid_constant__ CUtensorMap tm_dv,
+               const __grid_constant__ CUtensorMap tm_part, const BwdParams prm) {
   using Sm = BwdSmem<NCH>;
   constexpr int KVS = Sm::KVS;
   constexpr int QS = Sm::QS;
-  static_assert(!RESIDENT || NCH == 1, "resident mode keeps two dQ tiles of <= 64 columns");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Sm* smp = aligned_smem<Sm>(smem_raw);
   if (smp == nullptr) return;
@@ -108,13 +147,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int DP = (D + 15) & ~15;
   const int ksteps = DP >> 4;
   const int nqt = prm.nqt;
-  // Work units: resident mode = one head (all key tiles), walked persistently
-  // (unit = blockIdx.x, blockIdx.x + gridDim.x, ...); atomic mode = one
-  // (head, key tile) per CTA.
-  const int nunits = RESIDENT ? prm.BH : prm.BH * prm.nkv;
-  const int nj = RESIDENT ? prm.nkv : 1;
-  auto unit_head = [&](int u) { return RESIDENT ? u : u / prm.nkv; };
-  auto unit_j0 = [&](int u) { return RESIDENT ? 0 : u - (u / prm.nkv) * prm.nkv; };
+  const int nunits = prm.BH * prm.nkv;   // unit u = (head u / nkv, key tile u % nkv)
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
@@ -131,9 +164,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&sm.st_full, 1);
     mbar_init(&sm.ds_full, 1);
     mbar_init(&sm.mm_done, 1);
-    mbar_init(&sm.tm_free, 1);
-    mbar_init(&sm.acc_free, 1);
+    mbar_init(&sm.st_free, 1);
     mbar_init(&sm.dq_free, 1);
+    mbar_init(&sm.acc_free, 1);
+    for (int s = 0; s < kUnitRing; ++s) {
+      mbar_init(&sm.unit_full[s], 1);
+      mbar_init(&sm.unit_empty[s], 1 + kComputeThreads);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -146,6 +183,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + DP;
+  const uint32_t tDQ = (256 + 3 * DP <= 512) ? tmem + 256 + 2 * DP : tDPT;
+  constexpr bool kAhead = (QS == 2);   // S^T/dP^T of t + 1 ahead of t's gradient products
+  // Number of 16-token steps of tile t that hold tokens (8 for a full tile):
+  // products skip the steps of a last tile that are only padding.
+  auto valid16 = [&](int t) -> int { return min(8, (N - t * kTile + 15) >> 4); };
+
+  // The n-th claimed unit of this CTA (-1: no more work, or aborting).
+  auto next_unit = [&](int n) -> int {
+    const int slot = n % kUnitRing;
+    mbar_wait(&sm.unit_full[slot], (n / kUnitRing) & 1, abort_flag);
+    const int u = *abort_flag ? -1 : *reinterpret_cast<volatile int*>(&sm.unit[slot]);
+    mbar_arrive(&sm.unit_empty[slot]);
+    return u;
+  };
 
   if (warp < 4) {
   setmaxnreg_dec<kRegsCtl>();
@@ -156,39 +207,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      tma_prefetch_desc(&tm_o);
-      int qi = 0, kvi = 0;
-      for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-        const int bh = unit_head(u), j0 = unit_j0(u);
-        if (RESIDENT) {
-          // O rows feed Delta in the compute warps: pull this head's and the
-          // next head's O into L2 ahead of those loads.
-          for (int i = 0; i < nqt; ++i) {
-            for (int c = 0; c < NCH; ++c) {
-              if (u == (int)blockIdx.x) tma_prefetch_l2_3d(&tm_o, c * kChunkCols, i * kTile, bh);
-              if (u + (int)gridDim.x < nunits)
-                tma_prefetch_l2_3d(&tm_o, c * kChunkCols, i * kTile, unit_head(u + gridDim.x));
-            }
-          }
+      int qi = 0;
+      for (int n = 0;; ++n) {
+        const int slot = n % kUnitRing;
+        mbar_wait(&sm.unit_empty[slot], ((n / kUnitRing) & 1) ^ 1, abort_flag);
+        int u = atomicAdd(prm.ticket, 1);
+        if (u >= nunits || *abort_flag) u = -1;
+        sm.unit[slot] = u;
+        mbar_arrive(&sm.unit_full[slot]);
+        if (u < 0) break;
+        const int bh = u / prm.nkv, j = u - bh * prm.nkv, ks = n % KVS;
+        mbar_wait(&sm.kv_empty[ks], ((n / KVS) & 1) ^ 1, abort_flag);
+        mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+          tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
         }
-        for (int jj = 0; jj < nj; ++jj, ++kvi) {
-          const int j = j0 + jj, ks = kvi % KVS;
-          mbar_wait(&sm.kv_empty[ks], ((kvi / KVS) & 1) ^ 1, abort_flag);
-          mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
+        for (int i = 0; i < nqt; ++i, ++qi) {
+          const int qs = qi % QS;
+          mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
           for (int c = 0; c < NCH; ++c) {
-            tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
-            tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
-          }
-          for (int i = 0; i < nqt; ++i) {
-            if (RESIDENT && jj > 0) continue;
-            const int qs = qi % QS;
-            mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
-            mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
-            for (int c = 0; c < NCH; ++c) {
-              tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
-              tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
-            }
-            ++qi;
+            tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+            tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
           }
         }
       }
@@ -197,74 +238,93 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr bool kBf = Elt<T>::kBf16;
-      const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);   // S^T, dP^T
       const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
       const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
-      int it = 0, qi = 0, kvi = 0, hl = 0;
-      for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++hl) {
-        const int qbase = qi;
-        for (int jj = 0; jj < nj; ++jj, ++kvi) {
-          const int ks = kvi % KVS;
-          for (int i = 0; i < nqt; ++i) {
-            const bool fresh = !(RESIDENT && jj > 0);
-            const int qs = RESIDENT ? (qbase + i) % QS : qi % QS;
-            mbar_wait(&sm.kq_ready, it & 1, abort_flag);
-            tc_fence_after();
-            if (it > 0) {
-              mbar_wait(&sm.tm_free, (it - 1) & 1, abort_flag);
-              tc_fence_after();
-            }
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const int c = kk >> 2;
-              const uint32_t koff = (kk & 3) * 32;
-              mma_ss(tST, sw128_desc(smem_u32(sm.k[ks][c]) + koff, 16, 1024),
-                     sw128_desc(smem_u32(sm.q[qs][c]) + koff, 16, 1024), idS, kk > 0);
-            }
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const int c = kk >> 2;
-              const uint32_t koff = (kk & 3) * 32;
-              mma_ss(tDPT, sw128_desc(smem_u32(sm.v[ks][c]) + koff, 16, 1024),
-                     sw128_desc(smem_u32(sm.dO[qs][c]) + koff, 16, 1024), idS, kk > 0);
-            }
-            mma_commit(&sm.st_full);
-            mbar_wait(&sm.ds_full, it & 1, abort_flag);
-            tc_fence_after();
-            if (i == 0 && kvi > 0) {
-              // dV/dK of the previous key tile have been read out.
-              mbar_wait(&sm.acc_free, (kvi - 1) & 1, abort_flag);
-              tc_fence_after();
-            }
-            if (RESIDENT && jj == 0 && i == 0 && hl > 0) {
-              // dQ of the previous head has been read out.
-              mbar_wait(&sm.dq_free, (hl - 1) & 1, abort_flag);
-              tc_fence_after();
-            }
-            for (int kk = 0; kk < kTile / 16; ++kk) {
-              const uint32_t aoff = (kk & 3) * 32;
-              const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-              // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
-              mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
-                     sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV,
-                     acc);
-              // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
-              mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
-                     sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV,
-                     acc);
-            }
-            // dQ^ (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d] MN-major.
-            const uint32_t tDQ = RESIDENT ? (tmem + 384 + 64 * i) : tDPT;
-            for (int kk = 0; kk < kTile / 16; ++kk) {
-              const uint32_t acc =
-                  RESIDENT ? ((jj == 0 && kk == 0) ? 0u : 1u) : (kk > 0 ? 1u : 0u);
-              mma_ss(tDQ, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
-                     sw128_desc(smem_u32(sm.k[ks][0]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
-            }
-            mma_commit(&sm.mm_done);
-            if (!RESIDENT || jj == nj - 1) mma_commit(&sm.q_empty[qs]);
-            if (i == nqt - 1) mma_commit(&sm.kv_empty[ks]);
-            ++it;
-            if (fresh) ++qi;
+      // Iteration t = (unit n, query tile i); key tile j of the unit.
+      int n = 0, i = 0, t = 0, j = 0;
+      int u = next_unit(0);
+      auto issue_st = [&](int n_, int i_, int t_) {
+        const int ks = n_ % KVS, qs = t_ % QS;
+        mbar_wait(&sm.kq_ready, t_ & 1, abort_flag);
+        tc_fence_after();
+        const uint32_t idS = idesc_f16(kBf, 128, 16 * valid16(i_), false, false);
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const int c = kk >> 2;
+          const uint32_t koff = (kk & 3) * 32;
+          mma_ss(tST, sw128_desc(smem_u32(sm.k[ks][c]) + koff, 16, 1024),
+                 sw128_desc(smem_u32(sm.q[qs][c]) + koff, 16, 1024), idS, kk > 0);
+        }
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const int c = kk >> 2;
+          const uint32_t koff = (kk & 3) * 32;
+          mma_ss(tDPT, sw128_desc(smem_u32(sm.v[ks][c]) + koff, 16, 1024),
+                 sw128_desc(smem_u32(sm.dO[qs][c]) + koff, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(&sm.st_full);
+      };
+      auto issue_grads = [&](int n_, int i_, int t_, int j_) {
+        const int ks = n_ % KVS, qs = t_ % QS;
+        mbar_wait(&sm.ds_full, t_ & 1, abort_flag);
+        tc_fence_after();
+        if (i_ == 0 && n_ > 0) {
+          mbar_wait(&sm.acc_free, (n_ - 1) & 1, abort_flag);   // previous unit's dV/dK read out
+          tc_fence_after();
+        }
+        if (t_ > 0) {
+          mbar_wait(&sm.dq_free, (t_ - 1) & 1, abort_flag);    // previous dQ^ share read out
+          tc_fence_after();
+        }
+        const int kq = valid16(i_), kkeys = valid16(j_);
+        for (int kk = 0; kk < kq; ++kk) {
+          const uint32_t aoff = (kk & 3) * 32;
+          const uint32_t acc = (i_ == 0 && kk == 0) ? 0u : 1u;
+          // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
+          mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
+                 sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
+          // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
+          mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
+                 sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
+        }
+        // dQ^_j = dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d]
+        // MN-major. Key rows past N hold zero K^ rows and contribute nothing.
+        for (int kk = 0; kk < kkeys; ++kk) {
+          mma_ss(tDQ, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
+                 sw128_desc(smem_u32(sm.k[ks][0]) + kk * 2048, kChunkBytes, 1024), idQ,
+                 kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&sm.mm_done);
+        mma_commit(&sm.q_empty[qs]);
+        if (i_ == nqt - 1) mma_commit(&sm.kv_empty[ks]);
+      };
+      if (u >= 0) {
+        j = u % prm.nkv;
+        issue_st(n, i, t);
+        while (true) {
+          // The iteration after t (same unit, or the next claimed unit).
+          int n2 = n, i2 = i + 1, u2 = u;
+          if (i2 == nqt) {
+            n2 = n + 1;
+            i2 = 0;
+            u2 = next_unit(n2);
           }
+          const bool more = u2 >= 0;
+          if (kAhead && more) {
+            mbar_wait(&sm.st_free, t & 1, abort_flag);       // S^T/dP^T of t in registers
+            tc_fence_after();
+            issue_st(n2, i2, t + 1);
+          }
+          issue_grads(n, i, t, j);
+          if (!kAhead && more) {
+            mbar_wait(&sm.st_free, t & 1, abort_flag);
+            tc_fence_after();
+            issue_st(n2, i2, t + 1);
+          }
+          if (!more) break;
+          n = n2;
+          i = i2;
+          u = u2;
+          j = u % prm.nkv;
+          ++t;
         }
       }
     }
@@ -274,8 +334,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ------------------------------------------------------------ compute warps
     // Two warpgroups (warps 4..11). For TMEM reads a thread owns row r (its
     // lane quarter wq); warpgroup g takes S/dP columns [64g, 64g + 64) and
-    // every other 16-column block of the epilogue tiles. Warp-per-row phases
-    // (rotation, Delta, drains) give each of the 8 warps 16 rows.
+    // every other 16-column block of the gradient tiles. Warp-per-row phases
+    // (rotation, Delta) give each of the 8 warps 16 rows.
     constexpr int RW = kRowsPerWarp;
     const int cw = warp - 4;                       // compute warp 0..7
     const int g = cw >> 2;                         // warpgroup 0..1
@@ -285,47 +345,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const bool leader = threadIdx.x == 128;
     const float c2 = prm.c2;
-    int bh = 0, j0 = 0;          // current unit (set at the top of the unit loop)
-    int it = 0, qi = 0, kvi = 0, hl = 0;  // running iteration / load / unit counters
-    size_t head_row0 = 0;
+    constexpr int kBlk = 4 * NCH;                  // 16-column blocks of a gradient row
 
-    // Resident mode: this warp always handles the same 16-row slices of token
-    // tiles 0 and 1, so its table values are the same for every head; they
-    // are loaded once and kept in registers for the kernel's lifetime.
-    RopeQ<NCH, RW> tab[RESIDENT ? 2 : 1];
-    if (RESIDENT) {
-#pragma unroll
-      for (int t = 0; t < (RESIDENT ? 2 : 1); ++t)
-        load_rope_q<NCH, RW>(tab[t], rw0, t * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp,
-                             lane);
-    }
-
-    // Rotate key tile j_ (the kvi_-th key/value load) in its stage.
-    auto prep_k = [&](int j_, int kvi_) {
-      if (RESIDENT) {
-        mbar_wait(&sm.kv_full[kvi_ % KVS], (kvi_ / KVS) & 1, abort_flag);
-        if (j_ & 1) apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, tab[RESIDENT ? 1 : 0], lane);
-        else apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, tab[0], lane);
-      } else {
-        RopeQ<NCH, RW> rope;
-        load_rope_q<NCH, RW>(rope, rw0, j_ * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-        mbar_wait(&sm.kv_full[kvi_ % KVS], (kvi_ / KVS) & 1, abort_flag);
-        apply_rope_q<T, NCH, RW>(&sm.k[kvi_ % KVS][0][0], rw0, D, rope, lane);
-      }
+    // Rotate the key tile of the n_-th unit (key tile j_) in its stage.
+    auto prep_k = [&](int j_, int n_) {
+      RopeQ<NCH, RW> rope;
+      load_rope_q<NCH, RW>(rope, rw0, j_ * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.kv_full[n_ % KVS], (n_ / KVS) & 1, abort_flag);
+      apply_rope_q<T, NCH, RW>(&sm.k[n_ % KVS][0][0], rw0, D, rope, lane);
     };
-    // Prepare query tile i_ in stage qs_ (the qi_-th query load): lse2 (+inf
-    // for padded rows, so their P is exactly 0), rotation of Q, and Delta.
-    auto prep_q = [&](int i_, int qs_, int qi_) {
+    // Prepare query tile i_ of head bh_ (key tile j_) in stage t_ % QS
+    // (iteration t_): lse2 (+inf for padded rows, so their P is exactly 0),
+    // rotation of Q, and Delta; then tell the MMA warp.
+    auto prep_q = [&](int bh_, int j_, int i_, int t_) {
+      const int qs_ = t_ % QS;
+      const size_t row0 = static_cast<size_t>(bh_) * N;
       const int q0_ = i_ * kTile;
       if (g == 0) {
         const bool qv = (q0_ + r) < N;
-        sm.lse2[qs_][r] = qv ? prm.lse[head_row0 + q0_ + r] * 1.4426950408889634f : INFINITY;
+        sm.lse2[qs_][r] = qv ? prm.lse[row0 + q0_ + r] * 1.4426950408889634f : INFINITY;
       }
       // O granules of this warp's query rows (quad layout), read before the
       // tile wait so the load overlaps it.
-      const bool dpre = !RESIDENT && prm.delta_in != nullptr;
-      if (dpre && g == 0)
-        sm.delta[qs_][r] = (q0_ + r) < N ? prm.delta_in[head_row0 + q0_ + r] : 0.f;
+      const bool dpre = prm.delta_in != nullptr;
+      if (dpre && g == 0) sm.delta[qs_][r] = (q0_ + r) < N ? prm.delta_in[row0 + q0_ + r] : 0.f;
       const int rq = lane >> 3, gl = lane & 7;
       uint4 og[NCH][RW / 4];
 #pragma unroll
@@ -335,22 +378,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int tok = q0_ + rw0 + 4 * k + rq, gg = gl + 8 * h;
           og[h][k] = (!dpre && tok < N && 8 * gg < D)
                          ? __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(prm.o) +
-                                                                (head_row0 + tok) * D) + gg)
+                                                                (row0 + tok) * D) + gg)
                          : make_uint4(0u, 0u, 0u, 0u);
         }
-      if (RESIDENT) {
-        if (hl == 1 && i_ == 0) FRSA_STAMP(18);
-        mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
-        if (hl == 1 && i_ == 0) FRSA_STAMP(19);
-        if (i_ & 1) apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, tab[RESIDENT ? 1 : 0], lane);
-        else apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, tab[0], lane);
-      } else {
-        RopeQ<NCH, RW> rope;
-        load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-        mbar_wait(&sm.q_full[qs_], (qi_ / QS) & 1, abort_flag);
-        apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
-      }
-      if (hl == 1 && i_ == 0) FRSA_STAMP(20);
+      RopeQ<NCH, RW> rope;
+      load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      mbar_wait(&sm.q_full[qs_], (t_ / QS) & 1, abort_flag);
+      apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
       // Delta = sum_d O dO per query row: each lane dots its granule of O with
       // the same granule of the (unrotated) dO tile; 8 lanes share a row.
       const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
@@ -376,104 +410,160 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (gl == 0) {
           const int rr = rw0 + 4 * k + rq;
           sm.delta[qs_][rr] = dl;
-          if (prm.delta_out != nullptr && j0 == 0 && q0_ + rr < N)
-            prm.delta_out[head_row0 + q0_ + rr] = dl;
+          if (prm.delta_out != nullptr && j_ == 0 && q0_ + rr < N)
+            prm.delta_out[row0 + q0_ + rr] = dl;
         }
       }
-      if (hl == 1 && i_ == 0) FRSA_STAMP(21);
+      fence_proxy_async_smem();
+      named_bar(1, kComputeThreads);
+      if (leader) mbar_arrive(&sm.kq_ready);
     };
 
-    // Per unit: the first iteration's operands, then one iteration of
-    // look-ahead: the next key/query tile is prepared while the tensor core
-    // computes S^T and dP^T.
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++hl) {
-    bh = unit_head(u);
-    j0 = unit_j0(u);
-    head_row0 = static_cast<size_t>(bh) * N;
-    const int qbase = qi, kvbase = kvi, itbase = it;
-    (void)itbase;  // used by trace stamps only
-    if (hl == 1) FRSA_STAMP(16);
-    prep_k(j0, kvbase);
-    if (hl == 1) FRSA_STAMP(17);
-    prep_q(0, qi % QS, qi);
-    ++qi;
-    int cur_qs = qbase % QS;
-    fence_proxy_async_smem();
-    named_bar(1, kComputeThreads);
-    if (leader) mbar_arrive(&sm.kq_ready);
-    for (int jj = 0; jj < nj; ++jj) {
-      const int j = j0 + jj;
-      const int kv0 = j * kTile;
-      for (int i = 0; i < nqt; ++i) {
-        const int q0 = i * kTile;
-        const int qs = cur_qs;
-        const bool has_next = (i + 1 < nqt) || (jj + 1 < nj);
-        // Look-ahead needs the next query tile in a different stage: with one
-        // stage it can only arrive after this iteration's MMAs, so it is
-        // prepared after them instead (prep_late).
-        auto prep_next = [&]() {
-          const int nj_ = (i + 1 < nqt) ? jj : jj + 1;
-          const int ni = (i + 1 < nqt) ? i + 1 : 0;
-          if (ni == 0) prep_k(j0 + nj_, kvbase + nj_);
-          const bool nfresh = !(RESIDENT && nj_ > 0);
-          const int nqs = RESIDENT ? (qbase + ni) % QS : qi % QS;
-          if (nfresh) {
-            prep_q(ni, nqs, qi);
-            ++qi;
-          }
-          cur_qs = nqs;
-        };
-        const bool prep_late = has_next && (QS == 1 || KVS == 1);
-        if (has_next && !prep_late) prep_next();
-        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 0);
+    // Results of finished iterations leave through shared-memory tiles and
+    // TMA stores issued by the leader thread:
+    //   dV, dK = R^T dK^ scale   bf16 tiles [128 key][64] (128-byte swizzle)
+    //                            -> tm_dv / tm_dk at (64 c, key tile, head)
+    //   dQ^ share * scale        f32 tiles [128 query][32] (128-byte swizzle)
+    //                            -> tm_part at (32 h, query tile, slot * BH + head),
+    //                            a plain store for the first key tile of the
+    //                            slot, else an L2 reduce-add (after its turn).
+    // The share's completion (and its turn release and arrival count) is
+    // collected at the start of the next drain, so the leader does not wait
+    // for its own stores in between.
+    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
+    const uint32_t stb = smem_u32(stage);
+    const int S = prm.nslot;
+    const size_t head_elems = static_cast<size_t>(N) * D;
+    const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
+    int pend_bh = -1, pend_j = 0, pend_i = 0;   // dQ share whose store is in flight
 
-        mbar_wait(&sm.st_full, it & 1, abort_flag);
-        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 1);
-        tc_fence_after();
-        if (it > 0) mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);  // P/dS tiles free
-        {
-          // This warpgroup's 64 columns: S^T and dP^T loaded at once. Padded
-          // query columns have lse2 = +inf (P = 0, dS = 0); padded key rows
-          // only reach dV/dK rows that are never stored and dQ through zero
-          // K^ rows, so no per-element masking is needed.
-          float sv[2][32], dp[2][32];
-          tmem_ld32(tST + lane_off + g * 64, sv[0]);
-          tmem_ld32(tST + lane_off + g * 64 + 32, sv[1]);
-          tmem_ld32(tDPT + lane_off + g * 64, dp[0]);
-          tmem_ld32(tDPT + lane_off + g * 64 + 32, dp[1]);
-          tmem_wait_ld();
-          const uint32_t pbase = smem_u32(sm.p[g]), dbase = smem_u32(sm.ds[g]);
-          const uint32_t lbase = smem_u32(&sm.lse2[qs][g * 64]);
-          const uint32_t ebase = smem_u32(&sm.delta[qs][g * 64]);
+    // Sum the slots of query tile i_ of head bh_ in slot order, un-rotate,
+    // store dQ (quad layout: 8 lanes per 128-byte row segment), then drop the
+    // slots' lines from L2 without a write-back.
+    auto reduce_tile = [&](int bh_, int i_) {
+      __threadfence();
+      const int rq = lane >> 3, gl = lane & 7;
+      const int q0 = i_ * kTile;
+      T* dq_head = reinterpret_cast<T*>(prm.dq) + static_cast<size_t>(bh_) * head_elems;
+      const float* part0 = prm.dq_part + static_cast<size_t>(bh_) * head_elems;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
+      for (int k = 0; k < RW / 4; ++k) {
+        const int rr = rw0 + 4 * k + rq, tk = q0 + rr;
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 l4 = lds_f4(lbase + (hh * 32 + c4 * 4) * 4);
-              const float4 d4 = lds_f4(ebase + (hh * 32 + c4 * 4) * 4);
-              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int c = c4 * 4 + e;
-                const float pv = ex2(fmaf(sv[hh][c], c2, -lv[e]));
-                sv[hh][c] = pv;
-                dp[hh][c] = pv * (dp[hh][c] - dv4[e]);
-              }
+        for (int h = 0; h < NCH; ++h) {
+          const int gg = gl + 8 * h;
+          if (tk < N && 8 * gg < D) {
+            const float4* src =
+                reinterpret_cast<const float4*>(part0 + static_cast<size_t>(tk) * D + 8 * gg);
+            float4 a = __ldcg(src), bq = __ldcg(src + 1);
+            float v[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+            for (int sl = 1; sl < S; ++sl) {
+              src += slot_stride / 4;
+              a = __ldcg(src);
+              bq = __ldcg(src + 1);
+              v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+              v[4] += bq.x; v[5] += bq.y; v[6] += bq.z; v[7] += bq.w;
             }
+            const int p2 = rope_pos(tk, N, prm.has_cls);
+            if (p2 >= 0) {
+              const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
+              unrotate8(v, __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
+                        __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gg));
+            }
+            *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) =
+                pack8<T>(v);
+          }
+        }
+      }
+      named_bar(1, kComputeThreads);
+      // Only lines wholly inside this tile's rows: a line shared with a
+      // neighbouring tile or head may still be live.
+      const int q_rows = min(kTile, N - q0);
+      const int tid = threadIdx.x - 128;
+      for (int sl = 0; sl < S; ++sl) {
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(part0 + sl * slot_stride +
+                                                         static_cast<size_t>(q0) * D);
+        const uintptr_t hi = lo + static_cast<uintptr_t>(q_rows) * D * 4;
+        const uintptr_t l0 = (lo + 127) & ~static_cast<uintptr_t>(127);
+        for (uintptr_t ln = l0 + 128 * static_cast<uintptr_t>(tid); ln + 128 <= hi;
+             ln += 128 * kComputeThreads)
+          discard_l2_line(reinterpret_cast<const void*>(ln));
+      }
+    };
+
+    // Collect the dQ share in flight: once it is in L2, release the slot's
+    // next turn and count this key tile in; the last key tile of the head to
+    // arrive completes the query tile's dQ.
+    auto finish_pending = [&]() {
+      if (pend_bh < 0) return;
+      if (leader) {
+        tma_store_wait_all();
+        __threadfence();
+        const int gen = pend_j / S;
+        if (pend_j + S < prm.nkv)
+          st_release_gpu(prm.turns + (static_cast<size_t>(pend_bh) * nqt + pend_i) * S +
+                             pend_j % S, gen + 1);
+        const int before = atomicAdd(prm.arrive + static_cast<size_t>(pend_bh) * nqt + pend_i, 1);
+        sm.last_arrival = (before == prm.nkv - 1);
+      }
+      named_bar(1, kComputeThreads);
+      if (sm.last_arrival) reduce_tile(pend_bh, pend_i);
+      pend_bh = -1;
+    };
+
+    // Results of a finished iteration (its products done, mm_done waited):
+    // this key tile's dQ^ share of query tile i_, and at the unit's last
+    // query tile the unit's dV and dK^ (thread = tile row for TMEM reads).
+    auto drain = [&](int bh_, int j_, int i_) {
+      finish_pending();   // also: the stage is free (that store has completed)
+      const bool unit_end = (i_ == nqt - 1);
+      // kAhead: the MMA warp's next dQ^ product waits for these columns, so
+      // they are read out (two 16-column blocks per thread) and released
+      // before anything else. Otherwise nothing waits on them until this
+      // drain is over and blocks are read one at a time.
+      constexpr int kHeld = kAhead ? kBlk / 2 : 1;
+      float qv[kHeld][16];
+      if (kAhead) {
 #pragma unroll
-            for (int g4 = 0; g4 < 4; ++g4) {
-              const uint32_t off = sw128_off(r, hh * 4 + g4);
-              uint4 w;
-              w.x = Elt<T>::pack(sv[hh][g4 * 8 + 0], sv[hh][g4 * 8 + 1]);
-              w.y = Elt<T>::pack(sv[hh][g4 * 8 + 2], sv[hh][g4 * 8 + 3]);
-              w.z = Elt<T>::pack(sv[hh][g4 * 8 + 4], sv[hh][g4 * 8 + 5]);
-              w.w = Elt<T>::pack(sv[hh][g4 * 8 + 6], sv[hh][g4 * 8 + 7]);
-              sts_u4(pbase + off, w);
-              w.x = Elt<T>::pack(dp[hh][g4 * 8 + 0], dp[hh][g4 * 8 + 1]);
-              w.y = Elt<T>::pack(dp[hh][g4 * 8 + 2], dp[hh][g4 * 8 + 3]);
-              w.z = Elt<T>::pack(dp[hh][g4 * 8 + 4], dp[hh][g4 * 8 + 5]);
-              w.w = Elt<T>::pack(dp[hh][g4 * 8 + 6], dp[hh][g4 * 8 + 7]);
-              sts_u4(dbase + off, w);
+        for (int b = 0; b < kHeld; ++b) {
+          const int c16 = g + 2 * b;
+          if (c16 * 16 < DP) tmem_ld16(tDQ + lane_off + c16 * 16, qv[b]);
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        named_bar(1, kComputeThreads);
+        if (leader) mbar_arrive(&sm.dq_free);
+      }
+      if (unit_end) {
+        // dV and dK = R^T dK^ scale of key tile j_ as bf16 tiles: dV chunk c
+        // at stage chunk c, dK chunk c at stage chunk NCH + c.
+        const int kv0 = j_ * kTile;
+        const int pos = rope_pos(kv0 + r, N, prm.has_cls);
+#pragma unroll 1
+        for (int c16 = g; c16 < kBlk; c16 += 2) {
+          if (c16 * 16 < DP) {
+            float v[16], k16[16];
+            tmem_ld16(tDV + lane_off + c16 * 16, v);
+            tmem_ld16(tDK + lane_off + c16 * 16, k16);
+            tmem_wait_ld();
+            const int c = c16 >> 2;
+#pragma unroll
+            for (int h8 = 0; h8 < 2; ++h8) {
+              const int col = c16 * 16 + 8 * h8;
+              float a[8], bk[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                a[e] = v[8 * h8 + e];
+                bk[e] = k16[8 * h8 + e] * prm.scale;
+              }
+              if (pos >= 0 && col < D) {
+                const size_t t0 = static_cast<size_t>(pos) * (D >> 1) + (col >> 1);
+                unrotate8(bk, __ldg(reinterpret_cast<const float4*>(prm.cosp + t0)),
+                          __ldg(reinterpret_cast<const float4*>(prm.sinp + t0)));
+              }
+              const uint32_t gr = static_cast<uint32_t>((c16 & 3) * 2 + h8);
+              sts_u4(stb + c * kChunkBytes + sw128_off(r, gr), pack8<T>(a));
+              sts_u4(stb + (NCH + c) * kChunkBytes + sw128_off(r, gr), pack8<T>(bk));
             }
           }
         }
@@ -481,140 +571,201 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         named_bar(1, kComputeThreads);
         if (leader) {
-          mbar_arrive(&sm.ds_full);
-          if (RESIDENT) {
-            mbar_arrive(&sm.tm_free);
-            if (has_next && !prep_late) mbar_arrive(&sm.kq_ready);
-          }
-        }
-        if (hl == 0) FRSA_STAMP(hl * 15 + (it - itbase) * 3 + 2);
-        if (!RESIDENT) {
-          // dQ^ partial of this (key tile, query tile): scale and add into the workspace.
-          mbar_wait(&sm.mm_done, it & 1, abort_flag);
-          tc_fence_after();
-          uint8_t* stage = &sm.p[0][0];  // P/dS tiles are free until the next iteration
-#pragma unroll 1
-          for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
-            if (c16 * 16 < DP) {
-              float v[16];
-              tmem_ld16(tDPT + lane_off + c16 * 16, v);
-              tmem_wait_ld();
-              stage_write16<NCH>(stage, r, c16, v);
+          mbar_arrive(&sm.acc_free);
+          for (int c = 0; c < NCH; ++c) {
+            if (c * 64 < D) {
+              tma_store_3d(&tm_dv, stage + c * kChunkBytes, c * kChunkCols, kv0, bh_);
+              tma_store_3d(&tm_dk, stage + (NCH + c) * kChunkBytes, c * kChunkCols, kv0, bh_);
             }
           }
-          named_bar(1, kComputeThreads);
-          {
-            const uint32_t sbase = smem_u32(stage);
-            const int rq = lane >> 3, gl = lane & 7;
+          tma_store_commit();
+          tma_store_wait_read();
+        }
+        named_bar(1, kComputeThreads);
+      }
+      // dQ^ share * scale -> f32 tiles [128][32]: column block c16 is half
+      // (c16 & 1) of tile c16 >> 1.
 #pragma unroll
-            for (int k = 0; k < RW / 4; ++k) {
-              const int rr = rw0 + 4 * k + rq, tok = q0 + rr;
+      for (int b = 0; b < kBlk / 2; ++b) {
+        const int c16 = g + 2 * b;
+        if (c16 * 16 < DP) {
+          float* qb = qv[kAhead ? b : 0];
+          if (!kAhead) {
+            tmem_ld16(tDQ + lane_off + c16 * 16, qv[0]);
+            tmem_wait_ld();
+          }
+          const uint32_t tile = stb + (c16 >> 1) * kChunkBytes;
 #pragma unroll
-              for (int h = 0; h < NCH; ++h) {
-                const int gg = gl + 8 * h;
-                if (tok < N && 8 * gg < D) {
-                  float v[8];
-                  stage_read8<NCH>(sbase, rr, gg, prm.scale, v);
-                  float4* dst = reinterpret_cast<float4*>(prm.dq_accum + (head_row0 + tok) * D + 8 * gg);
-                  atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
-                  atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], v[7]));
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t ch = static_cast<uint32_t>((c16 & 1) * 4 + e);
+            sts_f4(tile + sw128_off(r, ch),
+                   make_float4(qb[4 * e] * prm.scale, qb[4 * e + 1] * prm.scale,
+                               qb[4 * e + 2] * prm.scale, qb[4 * e + 3] * prm.scale));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar(1, kComputeThreads);
+      if (leader) {
+        if (!kAhead) mbar_arrive(&sm.dq_free);
+        const int slot = j_ % S, gen = j_ / S;
+        if (gen > 0)
+          flag_wait_geq(prm.turns + (static_cast<size_t>(bh_) * nqt + i_) * S + slot, gen,
+                        abort_flag);
+        const int z = slot * prm.BH + bh_;
+        for (int h = 0; 32 * h < D; ++h) {
+          if (gen > 0) tma_reduce_add_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i_ * kTile, z);
+          else tma_store_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i_ * kTile, z);
+        }
+        tma_store_commit();
+        // Without kAhead the stage is the P/dS tiles, rewritten next iteration.
+        if (!kAhead) tma_store_wait_read();
+      }
+      if (!kAhead) named_bar(1, kComputeThreads);
+      pend_bh = bh_;
+      pend_j = j_;
+      pend_i = i_;
+    };
+
+    // The iteration sequence, as the MMA warp walks it. With kAhead, an
+    // iteration's results are drained during the next iteration (after its
+    // P/dS are published); one extra pass drains the last one.
+    int n = 0, i = 0, t = 0;
+    int u = next_unit(0);
+    if (u >= 0) {
+      int bh = u / prm.nkv, j = u - bh * prm.nkv;
+      prep_k(j, n);
+      prep_q(bh, j, 0, 0);
+      int pbh = -1, pj = 0, pi = 0, pt = 0;   // iteration waiting to be drained
+      bool have = true;                               // iteration t exists
+      int n2 = 0, i2 = 0, u2 = -1, bh2 = 0, j2 = 0;
+      bool more = false;
+      while (true) {
+        if (have) {
+          n2 = n;
+          i2 = i + 1;
+          u2 = u;
+          if (i2 == nqt) {
+            n2 = n + 1;
+            i2 = 0;
+            u2 = next_unit(n2);
+          }
+          more = u2 >= 0;
+          bh2 = more ? u2 / prm.nkv : 0;
+          j2 = more ? u2 - bh2 * prm.nkv : 0;
+          if (kAhead && more) {
+            if (n2 != n) prep_k(j2, n2);
+            prep_q(bh2, j2, i2, t + 1);
+          }
+          // S^T, dP^T of iteration t -> registers; release the TMEM columns.
+          const int qs = t % QS;
+          const int ncol = 16 * valid16(i);
+          mbar_wait(&sm.st_full, t & 1, abort_flag);
+          tc_fence_after();
+          // P = exp2(S^T c2 - lse2), dS = P (dP^T - Delta), one 32-column half
+          // at a time. Padded query columns have lse2 = +inf (P = 0, dS = 0);
+          // padded key rows only reach dV/dK rows that are never stored and dQ
+          // through zero K^ rows, so no per-element masking is needed.
+          const uint32_t lbase = smem_u32(&sm.lse2[qs][g * 64]);
+          const uint32_t ebase = smem_u32(&sm.delta[qs][g * 64]);
+          const uint32_t pbase = smem_u32(sm.p[g]), dbase = smem_u32(sm.ds[g]);
+          uint32_t pk[2][16], dk[2][16];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float sv[32], dp[32];
+            const bool live = 64 * g + 32 * hh < ncol;
+            if (live) {
+              tmem_ld32(tST + lane_off + g * 64 + 32 * hh, sv);
+              tmem_ld32(tDPT + lane_off + g * 64 + 32 * hh, dp);
+            }
+            tmem_wait_ld();
+            if (hh == 1) {
+              // S^T/dP^T of iteration t are in registers: release the columns.
+              tc_fence_before();
+              named_bar(1, kComputeThreads);
+              if (leader) mbar_arrive(&sm.st_free);
+              // P/dS tiles are free once the previous iteration's products
+              // are done (non-kAhead: waited before this iteration began).
+              if (kAhead && t > 0) {
+                mbar_wait(&sm.mm_done, (t - 1) & 1, abort_flag);
+                tc_fence_after();
+              }
+              if (64 * g < ncol) {
+#pragma unroll
+                for (int g4 = 0; g4 < 4; ++g4) {
+                  const uint32_t off = sw128_off(r, g4);
+                  sts_u4(pbase + off, make_uint4(pk[0][4 * g4], pk[0][4 * g4 + 1],
+                                                 pk[0][4 * g4 + 2], pk[0][4 * g4 + 3]));
+                  sts_u4(dbase + off, make_uint4(dk[0][4 * g4], dk[0][4 * g4 + 1],
+                                                 dk[0][4 * g4 + 2], dk[0][4 * g4 + 3]));
                 }
               }
             }
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 l4 = lds_f4(lbase + (hh * 32 + c4 * 4) * 4);
+              const float4 d4 = lds_f4(ebase + (hh * 32 + c4 * 4) * 4);
+              const float p0 = ex2(fmaf(sv[4 * c4 + 0], c2, -l4.x));
+              const float p1 = ex2(fmaf(sv[4 * c4 + 1], c2, -l4.y));
+              const float p2 = ex2(fmaf(sv[4 * c4 + 2], c2, -l4.z));
+              const float p3 = ex2(fmaf(sv[4 * c4 + 3], c2, -l4.w));
+              pk[hh][2 * c4] = Elt<T>::pack(p0, p1);
+              pk[hh][2 * c4 + 1] = Elt<T>::pack(p2, p3);
+              dk[hh][2 * c4] = Elt<T>::pack(p0 * (dp[4 * c4 + 0] - d4.x),
+                                            p1 * (dp[4 * c4 + 1] - d4.y));
+              dk[hh][2 * c4 + 1] = Elt<T>::pack(p2 * (dp[4 * c4 + 2] - d4.z),
+                                                p3 * (dp[4 * c4 + 3] - d4.w));
+            }
           }
+          if (64 * g + 32 < ncol) {
+#pragma unroll
+            for (int g4 = 0; g4 < 4; ++g4) {
+              const uint32_t off = sw128_off(r, 4 + g4);
+              sts_u4(pbase + off, make_uint4(pk[1][4 * g4], pk[1][4 * g4 + 1], pk[1][4 * g4 + 2],
+                                             pk[1][4 * g4 + 3]));
+              sts_u4(dbase + off, make_uint4(dk[1][4 * g4], dk[1][4 * g4 + 1], dk[1][4 * g4 + 2],
+                                             dk[1][4 * g4 + 3]));
+            }
+          }
+          fence_proxy_async_smem();
           tc_fence_before();
           named_bar(1, kComputeThreads);
-          if (leader) {
-            mbar_arrive(&sm.tm_free);
-            if (has_next && !prep_late) mbar_arrive(&sm.kq_ready);
-          }
+          if (leader) mbar_arrive(&sm.ds_full);
         }
-        if (prep_late) {
-          prep_next();
-          fence_proxy_async_smem();
-          named_bar(1, kComputeThreads);
-          if (leader) mbar_arrive(&sm.kq_ready);
+        // Drain: kAhead the previous iteration (its products finished before
+        // this iteration's P/dS store; on the extra pass wait here), else this one.
+        if (!kAhead) {
+          mbar_wait(&sm.mm_done, t & 1, abort_flag);
+          tc_fence_after();
+          pbh = bh; pj = j; pi = i; pt = t;
+        } else if (!have && pbh >= 0) {
+          mbar_wait(&sm.mm_done, pt & 1, abort_flag);
+          tc_fence_after();
         }
-        ++it;
+        if (pbh >= 0) drain(pbh, pj, pi);
+        if (!have) break;
+        if (!kAhead && more) {
+          if (n2 != n) prep_k(j2, n2);
+          prep_q(bh2, j2, i2, t + 1);
+        }
+        if (kAhead) {
+          pbh = bh; pj = j; pi = i; pt = t;
+        }
+        if (!more) {
+          if (!kAhead) break;
+          have = false;
+          continue;
+        }
+        n = n2;
+        i = i2;
+        u = u2;
+        bh = bh2;
+        j = j2;
+        ++t;
       }
-      // dV, dK epilogue of key tile j
-      RopeQ<NCH, RW> rope_k;
-      if (!RESIDENT) load_rope_q<NCH, RW>(rope_k, rw0, kv0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.mm_done, (it - 1) & 1, abort_flag);
-      tc_fence_after();
-      {
-        // TMEM rows -> f32 staging (P/dS tiles, free now) -> warp-per-row drain.
-        uint8_t* stage_v = &sm.p[0][0];
-        uint8_t* stage_k = (NCH == 1) ? &sm.ds[0][0] : &sm.p[0][0];
-        T* dv_head = reinterpret_cast<T*>(prm.dv) + head_row0 * D;
-        T* dk_head = reinterpret_cast<T*>(prm.dk) + head_row0 * D;
-#pragma unroll 1
-        for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
-          if (c16 * 16 < DP) {
-            float v[16];
-            tmem_ld16(tDV + lane_off + c16 * 16, v);
-            tmem_wait_ld();
-            stage_write16<NCH>(stage_v, r, c16, v);
-          }
-        }
-        if (NCH != 1) {
-          named_bar(1, kComputeThreads);
-          drain_q<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, static_cast<const RopeQ<NCH, RW>*>(nullptr), dv_head, lane);
-          named_bar(1, kComputeThreads);
-        }
-#pragma unroll 1
-        for (int c16 = g; c16 < 4 * NCH; c16 += 2) {
-          if (c16 * 16 < DP) {
-            float v[16];
-            tmem_ld16(tDK + lane_off + c16 * 16, v);
-            tmem_wait_ld();
-            stage_write16<NCH>(stage_k, r, c16, v);
-          }
-        }
-        named_bar(1, kComputeThreads);
-        if (NCH == 1)
-          drain_q<T, NCH, RW>(stage_v, rw0, kv0, N, D, 1.f, static_cast<const RopeQ<NCH, RW>*>(nullptr), dv_head, lane);
-        if (RESIDENT && (j & 1))
-          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &tab[RESIDENT ? 1 : 0], dk_head, lane);
-        else if (RESIDENT)
-          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &tab[0], dk_head, lane);
-        else
-          drain_q<T, NCH, RW>(stage_k, rw0, kv0, N, D, prm.scale, &rope_k, dk_head, lane);
-      }
-      tc_fence_before();
-      named_bar(1, kComputeThreads);
-      if (leader) mbar_arrive(&sm.acc_free);
-      if (hl == 0) FRSA_STAMP(hl * 15 + 12 + jj);
-      ++kvi;
+      finish_pending();
     }
-    if (RESIDENT) {
-      // dQ epilogue: every MMA has completed (last mm_done waited above).
-      uint8_t* stage = &sm.p[0][0];
-      T* dq_head = reinterpret_cast<T*>(prm.dq) + head_row0 * D;
-      for (int i = 0; i < nqt; ++i) {
-
-#pragma unroll 1
-        for (int c16 = g; c16 < 4; c16 += 2) {
-          if (c16 * 16 < DP) {
-            float v[16];
-            tmem_ld16(tmem + 384 + 64 * i + lane_off + c16 * 16, v);
-            tmem_wait_ld();
-            stage_write16<NCH>(stage, r, c16, v);
-          }
-        }
-        named_bar(1, kComputeThreads);
-        if (i & 1)
-          drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &tab[RESIDENT ? 1 : 0],
-                              dq_head, lane);
-        else
-          drain_q<T, NCH, RW>(stage, rw0, i * kTile, N, D, prm.scale, &tab[0], dq_head, lane);
-        tc_fence_before();
-        named_bar(1, kComputeThreads);
-      }
-      if (leader) mbar_arrive(&sm.dq_free);
-      if (hl == 0) FRSA_STAMP(hl * 15 + 14);
-    }
-    }  // unit loop
   }
 
   FRSA_STAMP(30);
@@ -626,7 +777,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// dQ = R^T dQ^ (dQ^ already scaled), one thread per 8 columns.
 // Delta = rowsum(dO * O) in f32 for every row of [B*H*N, D]: 8 lanes per
 // row, one 16-byte granule each per step (fa_rope_full .py:352-357).
 template <typename T>
@@ -655,76 +805,56 @@ __global__ void delta_rows_kernel(const T* __restrict__ o, const T* __restrict__
   if (gl == 0 && row < rows) delta[row] = acc;
 }
 
-template <typename T>
-__global__ void dq_finalize_kernel(const float* __restrict__ acc, T* __restrict__ dq,
-                                   const float* __restrict__ cosp, const float* __restrict__ sinp,
-                                   long long rows, int N, int D, int has_cls) {
-  const int gpr = D >> 3;
-  const long long gidx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (gidx >= rows * gpr) return;
-  const long long row = gidx / gpr;
-  const int g = static_cast<int>(gidx - row * gpr);
-  const int t = static_cast<int>(row % N);
-  const float4* src = reinterpret_cast<const float4*>(acc + row * D + g * 8);
-  float v[8];
-  const float4 a = src[0], b = src[1];
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  const int pos = rope_pos(t, N, has_cls);
-  if (pos >= 0) {
-    const int D2 = D >> 1;
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float c = __ldg(cosp + static_cast<size_t>(pos) * D2 + g * 4 + p);
-      const float s = __ldg(sinp + static_cast<size_t>(pos) * D2 + g * 4 + p);
-      const float e = v[2 * p], od = v[2 * p + 1];
-      v[2 * p] = e * c + od * s;
-      v[2 * p + 1] = od * c - e * s;
-    }
-  }
-  uint4 w;
-  w.x = Elt<T>::pack(v[0], v[1]);
-  w.y = Elt<T>::pack(v[2], v[3]);
-  w.z = Elt<T>::pack(v[4], v[5]);
-  w.w = Elt<T>::pack(v[6], v[7]);
-  reinterpret_cast<uint4*>(dq + row * D)[g] = w;
-}
-
 }  // namespace
 
 bool bwd_needs_workspace(const LaunchShape& s) { return !(s.N <= 2 * kTile && s.D <= 64); }
 
+int bwd_slots(const LaunchShape& s) {
+  const int nkv = (s.N + kTile - 1) / kTile;
+  return nkv < kMaxDqSlots ? nkv : kMaxDqSlots;
+}
+
+size_t bwd_counter_ints(const LaunchShape& s, int nslot) {
+  const size_t nqt = (static_cast<size_t>(s.N) + kTile - 1) / kTile;
+  // arrival counters, slot turn counters, the claim ticket; 16-byte multiple
+  return (static_cast<size_t>(s.BH) * nqt * (1 + nslot) + 1 + 3) & ~static_cast<size_t>(3);
+}
+
 namespace {
 
-template <typename T, int NCH, bool RESIDENT>
+template <typename T, int NCH>
 cudaError_t launch_bwd_main(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                             const CUtensorMap& tm_v, const CUtensorMap& tm_do,
-                            const CUtensorMap& tm_o, const BwdParams& p, cudaStream_t stream) {
-  const size_t smem = sizeof(BwdSmem<NCH>) + 1024;
-  auto kern = bwd_kernel<T, NCH, RESIDENT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+                            const CUtensorMap& tm_o, const CUtensorMap& tm_dk,
+                            const CUtensorMap& tm_dv, const CUtensorMap& tm_part,
+                            const BwdParams& p, cudaStream_t stream) {
+  // The dynamic window starts 1024-aligned in practice; the slack is cut to
+  // what the 227 KiB limit leaves (aligned_smem reports a misfit).
+  constexpr size_t kMaxDyn = 232448;
+  const size_t smem = (sizeof(BwdSmem<NCH>) + 1024 <= kMaxDyn) ? sizeof(BwdSmem<NCH>) + 1024
+                                                                : kMaxDyn;
+  auto kern = bwd_kernel<T, NCH>;
+  cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
-  int nsm = 148;
-  {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  }
-  const long long grid = RESIDENT ? static_cast<long long>(s.BH < nsm ? s.BH : nsm)
-                                  : static_cast<long long>(s.BH) * p.nkv;
+  const long long nunits = static_cast<long long>(s.BH) * p.nkv;
+  const int nsm = device_sm_count();
+  const long long grid = nunits < nsm ? nunits : nsm;   // one CTA per SM (512 TMEM columns)
   kern<<<static_cast<unsigned>(grid), kBwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, tm_o,
-                                                                     p);
+                                                                     tm_dk, tm_dv, tm_part, p);
   return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                         const CUtensorMap& tm_v, const CUtensorMap& tm_do,
-                         const CUtensorMap& tm_o, const void* o,
-                         const CUtensorMap* tm_grads, const void* d_o, const float* lse,
-                         float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
-                         void* dv, float* dq_accum, float* delta_buf, cudaStream_t stream) {
+}  // namespace
+
+cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
+                               const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                               const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                               const CUtensorMap& tm_dk, const CUtensorMap& tm_dv,
+                               const CUtensorMap& tm_part, const void* o,
+                               const void* d_o, const float* lse, float* delta,
+                               const float* cosp, const float* sinp, void* dq, void* dk, void* dv,
+                               float* dq_part, int nslot, int* counters, float* delta_buf,
+                               cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
   BwdParams p;
   p.cosp = cosp;
@@ -735,58 +865,52 @@ cudaError_t launch_bwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
-  p.dq_accum = dq_accum;
+  p.dq_part = dq_part;
+  p.nslot = nslot;
   p.BH = s.BH;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
   p.nkv = p.nqt;
+  p.arrive = counters;
+  p.turns = counters + static_cast<size_t>(s.BH) * p.nqt;
+  p.ticket = p.turns + static_cast<size_t>(s.BH) * p.nqt * nslot;
   p.has_cls = s.has_cls;
   p.c2 = s.scale * 1.4426950408889634f;
   p.scale = s.scale;
-  cudaError_t e;
-  if (!bwd_needs_workspace(s)) {
-    if (tm_grads == nullptr) return cudaErrorInvalidValue;
-    return launch_bwd_small(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads, o, lse, delta, cosp, sinp,
-                            dq, dk, dv, stream);
-  }
-  e = cudaMemsetAsync(dq_accum, 0, static_cast<size_t>(rows) * s.D * sizeof(float), stream);
+  if (nslot < 1 || nslot > p.nkv) return cudaErrorInvalidValue;
+  // Counters and the claim ticket start at zero; the partial sums need no
+  // clearing (the first key tile of each slot stores its share).
+  cudaError_t e = cudaMemsetAsync(counters, 0, bwd_counter_ints(s, nslot) * sizeof(int), stream);
   if (e != cudaSuccess) return e;
   if (delta_buf != nullptr) {
     // Delta once per row here, instead of once per (key tile, query tile) in
     // the main kernel (which would also re-read O for every key tile).
     const long long threads_d = rows * 8;
-    delta_rows_kernel<T><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0, stream>>>(
-        static_cast<const T*>(o), static_cast<const T*>(d_o), delta_buf, rows, s.D);
+    if (s.bf16)
+      delta_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0,
+                                         stream>>>(static_cast<const __nv_bfloat16*>(o),
+                                                   static_cast<const __nv_bfloat16*>(d_o),
+                                                   delta_buf, rows, s.D);
+    else
+      delta_rows_kernel<__half><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0,
+                                  stream>>>(static_cast<const __half*>(o),
+                                            static_cast<const __half*>(d_o), delta_buf, rows, s.D);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     p.delta_in = delta_buf;
     p.delta_out = nullptr;   // delta_buf is the caller's delta when one was given
   }
-  e = (s.D > 64) ? launch_bwd_main<T, 2, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream)
-                 : launch_bwd_main<T, 1, false>(s, tm_q, tm_k, tm_v, tm_do, tm_o, p, stream);
-  if (e != cudaSuccess) return e;
-  const int threads = 256;
-  const long long total = rows * (s.D >> 3);
-  dq_finalize_kernel<T><<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
-                          stream>>>(dq_accum, static_cast<T*>(dq), cosp, sinp, rows, s.N, s.D,
-                                    s.has_cls);
-  return cudaGetLastError();
-}
-
-}  // namespace
-
-cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
-                       const void* o, const CUtensorMap* tm_grads,
-                       const void* d_o, const float* lse, float* delta, const float* cosp,
-                       const float* sinp, void* dq, void* dk, void* dv, float* dq_accum,
-                       float* delta_buf, cudaStream_t stream) {
   if (s.bf16)
-    return launch_bwd_t<__nv_bfloat16>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse,
-                                       delta, cosp, sinp, dq, dk, dv, dq_accum, delta_buf, stream);
-  return launch_bwd_t<__half>(s, tm_q, tm_k, tm_v, tm_do, tm_o, o, tm_grads, d_o, lse, delta, cosp,
-                              sinp, dq, dk, dv, dq_accum, delta_buf, stream);
+    return (s.D > 64)
+               ? launch_bwd_main<__nv_bfloat16, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                   tm_part, p, stream)
+               : launch_bwd_main<__nv_bfloat16, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                   tm_part, p, stream);
+  return (s.D > 64) ? launch_bwd_main<__half, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                 tm_part, p, stream)
+                    : launch_bwd_main<__half, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                 tm_part, p, stream);
 }
 
 }  // namespace frsa

@@ -568,12 +568,9 @@ cudaError_t launch_bwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
   // ~226 KiB layout under the 227 KiB limit (aligned_smem reports a misfit).
   const size_t smem = sizeof(BsSmem) + 256;
   auto kern = bwd_small_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
-  int nsm = 148, dev = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int nsm = device_sm_count();
   const int grid = s.BH < nsm ? s.BH : nsm;
   kern<<<grid, kBsThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_do, tm_o, tm_grads[0], tm_grads[1],
                                             tm_grads[2], p);

@@ -422,8 +422,7 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.c2 = s.scale * 1.4426950408889634f;
   const size_t smem = sizeof(FwdSmem<NCH>) + 1024;
   auto kern = fwd_kernel<T, NCH>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
   const long long units = static_cast<long long>(s.BH) * p.npair;
   kern<<<static_cast<unsigned>(units), kFwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, p);

@@ -388,19 +388,6 @@ __global__ void __launch_bounds__(kFsThreads, 1)
   }
 }
 
-int sm_count() {
-  static int cache[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
-  }
-  return cache[dev];
-}
-
 template <typename T>
 cudaError_t launch_fwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
                                const CUtensorMap& tm_k, const CUtensorMap& tm_v,
@@ -422,10 +409,10 @@ cudaError_t launch_fwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
   // the ~224 KiB layout under the 227 KiB limit (aligned_smem reports a misfit).
   const size_t smem = sizeof(FsSmem) + 256;
   auto kern = fwd_small_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
-  const int grid = s.BH < sm_count() ? s.BH : sm_count();
+  const int nsm = device_sm_count();
+  const int grid = s.BH < nsm ? s.BH : nsm;
   kern<<<grid, kFsThreads, smem, stream>>>(tm_q, tm_k, tm_v, p);
   return cudaGetLastError();
 }

@@ -65,17 +65,40 @@ cudaError_t launch_bwd_small(const LaunchShape& s, const CUtensorMap& tm_q,
                              float* delta, const float* cosp, const float* sinp, void* dq,
                              void* dk, void* dv, cudaStream_t stream);
 
-// Backward (delta preprocess + main kernel + optional dQ finalize).
-// dq_accum: fp32 [BH, N, D] workspace or nullptr when bwd_needs_workspace() is false.
-// tm_grads: maps over dQ, dK, dV (in that order), required when
-// bwd_needs_workspace() is false (the persistent kernel stores through them).
+// True when the shape needs the general backward (and its workspace): N > 256
+// or D > 64. Otherwise the persistent single-head kernel runs (launch_bwd_small).
 bool bwd_needs_workspace(const LaunchShape& s);
-cudaError_t launch_bwd(const LaunchShape& s, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                       const CUtensorMap& tm_v, const CUtensorMap& tm_do, const CUtensorMap& tm_o,
-                       const void* o, const CUtensorMap* tm_grads, const void* d_o, const float* lse,
-                       float* delta, const float* cosp, const float* sinp, void* dq, void* dk,
-                       void* dv, float* dq_accum, float* delta_buf, cudaStream_t stream);
-// delta_buf (atomic mode, optional): B*H*N floats that receive Delta in a
-// pre-pass, which the main kernel then reads instead of forming it per tile.
+// Partial dQ slots frsa_bwd uses for this shape (min(key tiles, 8)).
+int bwd_slots(const LaunchShape& s);
+// int32 words of counters (arrivals, slot turns, claim ticket) the general
+// backward needs with `nslot` partial slots.
+size_t bwd_counter_ints(const LaunchShape& s, int nslot);
+
+// General backward: optional Delta pre-pass into delta_buf (then read by the
+// main kernel; when null the kernel forms Delta itself and writes `delta` if
+// given), then the persistent key-tile kernel with the ordered dQ reduction.
+// dq_part: f32 [nslot, BH, N, D] partial sums (1 <= nslot <= key tiles);
+// counters: bwd_counter_ints(s, nslot) int32 words (cleared here on `stream`).
+// tm_dk / tm_dv: the usual maps over dK / dV; tm_part: f32 map {D, N, nslot*BH}
+// over dq_part with box {32, 128, 1} and the 128-byte swizzle.
+cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
+                               const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                               const CUtensorMap& tm_do, const CUtensorMap& tm_o,
+                               const CUtensorMap& tm_dk, const CUtensorMap& tm_dv,
+                               const CUtensorMap& tm_part, const void* o,
+                               const void* d_o, const float* lse, float* delta,
+                               const float* cosp, const float* sinp, void* dq, void* dk, void* dv,
+                               float* dq_part, int nslot, int* counters, float* delta_buf,
+                               cudaStream_t stream);
+
+// Number of SMs of the current device (queried once per device).
+int device_sm_count();
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+cudaError_t set_max_dynamic_smem_once(const void* kernel, size_t bytes);
+template <typename K>
+inline cudaError_t set_max_dynamic_smem_once(K* kernel, size_t bytes) {
+  return set_max_dynamic_smem_once(reinterpret_cast<const void*>(kernel), bytes);
+}
 
 }  // namespace frsa

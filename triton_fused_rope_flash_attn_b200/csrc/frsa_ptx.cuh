@@ -172,6 +172,41 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// ---------------------------------------------------------------- global flags
+// Acquire load / release store of a 32-bit flag in global memory (GPU scope).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Drop a 128-byte line (128-byte aligned) from L2 without writing it back:
+// for scratch whose contents are dead.
+__device__ __forceinline__ void discard_l2_line(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+// Wait until the flag at `p` (written by another CTA) reaches `target`.
+// Bounded like mbar_wait: gives up after FRSA_WAIT_LIMIT_NS, records
+// FRSA_DEV_TIMEOUT and raises the CTA's abort flag; returns false then.
+__device__ __forceinline__ bool flag_wait_geq(const int* p, int target, volatile int* abort_flag) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (*abort_flag != 0) return false;
+    if (globaltimer() - t0 > FRSA_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      atomicExch(&g_dev_status, FRSA_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -254,6 +289,23 @@ __device__ __forceinline__ void tma_store_commit() {
 // Wait until the shared-memory sources of all committed store groups have been read.
 __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// 3-D tiled reduce-add shared -> {x, y, z} (f32 elements added at L2; elements
+// outside the tensor are not touched), as one bulk group of the issuing thread.
+__device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, const void* smem_src, int x,
+                                                  int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+// Wait until all committed bulk groups of this thread have completed (their
+// global writes done), then order them before later generic-proxy accesses.
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05

@@ -241,13 +241,10 @@ cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMa
   p.nft = 3 * C / BN;
   const long long ntiles = ((M + kTile - 1) / kTile) * p.nft;
   p.ntiles = static_cast<int>(ntiles);
-  int nsm = 148, dev = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int nsm = device_sm_count();
   const dim3 grid(static_cast<unsigned>(ntiles < nsm ? ntiles : nsm));
   auto launch = [&](auto kern, size_t smem) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = set_max_dynamic_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, kQkvThreads, smem, stream>>>(tm_x, tm_w, p);
     return cudaGetLastError();

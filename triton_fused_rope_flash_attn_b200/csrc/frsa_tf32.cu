@@ -357,8 +357,7 @@ cudaError_t launch_fwd_tf32_t(const LaunchShape& s, const CUtensorMap& tm_q,
   p.c2 = s.scale * 1.4426950408889634f;
   const size_t smem = sizeof(T32FwdSmem<NC>) + 1024;
   auto kern = fwd_tf32_kernel<NC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
   const long long units = static_cast<long long>(s.BH) * p.nqt;
   kern<<<static_cast<unsigned>(units), kT32Threads, smem, stream>>>(tm_q, tm_k, tm_v, p);
@@ -853,8 +852,7 @@ cudaError_t launch_bwd_tf32_t(const LaunchShape& s, const CUtensorMap* maps, con
   {
     const size_t smem = sizeof(T32KvSmem<NC>) + 1024;
     auto kern = bwd_kv_tf32_kernel<NC>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    e = set_max_dynamic_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(static_cast<long long>(s.BH) * p.nkv), kT32Threads, smem,
            stream>>>(maps[2], maps[4], maps[0], maps[1], maps[5], maps[6], p);
@@ -864,8 +862,7 @@ cudaError_t launch_bwd_tf32_t(const LaunchShape& s, const CUtensorMap* maps, con
   {
     const size_t smem = sizeof(T32QSmem<NC>) + 1024;
     auto kern = bwd_q_tf32_kernel<NC>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    e = set_max_dynamic_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(static_cast<long long>(s.BH) * p.nqt), kT32Threads, smem,
            stream>>>(maps[0], maps[5], maps[2], maps[3], maps[4], p);
