@@ -9,9 +9,10 @@
  * through ctypes with torch-allocated device buffers.
  *
  * Conventions
- *   - All tensor pointers are device pointers. q, k, v, o, d_o, dq, dk, dv are
- *     contiguous [B, H, N, D] in the I/O dtype; lse and delta are contiguous
- *     fp32 [B, H, N]; cosp/sinp are contiguous fp32 [n_pos, D/2].
+ *   - All tensor pointers are device pointers. q, k, v are [B, H, N, D] in the
+ *     I/O dtype with unit d stride (contiguous unless *_strides say otherwise);
+ *     o, d_o, dq, dk, dv are contiguous [B, H, N, D]; lse and delta are
+ *     contiguous fp32 [B, H, N]; cosp/sinp are contiguous fp32 [n_pos, D/2].
  *   - Token t uses table row t - has_cls; token 0 is not rotated when has_cls.
  *   - scale multiplies the logits (the reference uses 1/sqrt(D)).
  *   - lse receives max + ln(sum) of the scaled logits per query row, the
@@ -82,7 +83,23 @@ typedef struct frsa_attn_args {
                              TF32 tensor-core products (frsa_bwd: D <= 64, and a Delta
                              workspace of B*H*N floats unless `delta` is given) */
   float scale;
+  /* Optional element strides (b, h, n) of q, k and v; the d stride is 1. All
+   * zero = contiguous [B, H, N, D]. Non-zero strides must be multiples of 16
+   * bytes (e.g. the q, k, v views of a [B, N, 3, H, D] projection output), and
+   * the pointers 16-byte aligned. Other tensors are always contiguous. */
+  int64_t q_strides[3];
+  int64_t k_strides[3];
+  int64_t v_strides[3];
+  /* FRSA_FLAG_* bits. */
+  int32_t flags;
 } frsa_attn_args;
+
+/* q and k arrive already rotated (e.g. by frsa_qkv_rope, which applies the
+ * RoPE in the projection's epilogue): the kernels skip every rotation, and
+ * frsa_bwd returns dq and dk with respect to the given q and k (no R^T).
+ * cosp/sinp may then be NULL and n_pos is not checked. No counterpart in the
+ * reference, whose kernels always rotate. */
+#define FRSA_FLAG_NO_ROPE 1
 
 /* Forward: O = softmax(R(Q) R(K)^T * scale) V and lse.
  * Replaces the _attn_fwd launch of TritonAttention.forward
@@ -94,8 +111,8 @@ int frsa_fwd(const frsa_attn_args* args, void* stream);
  * (_attn_bwd_preprocess fa_rope_full .py:1076-1082, _attn_bwd_dk_dv_rope
  * fa_rope_full .py:1084-1107, _attn_bwd_dq_rope fa_rope_full .py:1109-1136)
  * with one persistent kernel (N <= 256 and D <= 64), or otherwise with a
- * counter clear, a Delta pass and one persistent key-tile kernel whose dQ is
- * reduced over key tiles in a fixed order. Results are bitwise reproducible
+ * counter clear, a row pass (rotated Q and K, Delta) and one persistent
+ * key-tile kernel whose dQ is reduced over key tiles in a fixed order. Results are bitwise reproducible
  * from call to call in both cases. */
 int frsa_bwd(const frsa_attn_args* args, void* stream);
 
@@ -104,6 +121,7 @@ int frsa_bwd(const frsa_attn_args* args, void* stream);
  * T = ceil(N/128) key tiles and S = min(T, 8) partial-dQ slots,
  *   S * B*H*N*D floats (partial dQ sums)
  * + 4 * ((B*H*T*(1 + S) + 4) & ~3) bytes (arrival and slot counters, a claim ticket)
+ * + 2 * B*H*N*D 16-bit values (the rotated Q and K)
  * + B*H*N floats (Delta rows), the last term only when args->delta is NULL;
  * for F32 compute, B*H*N floats of Delta when args->delta is NULL.
  * ABI version 2 (version 1 asked for B*H*N*(D+1) floats in every case).

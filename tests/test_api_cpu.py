@@ -130,11 +130,11 @@ def test_bwd_requires_gradients_and_workspace(lib):
     assert lib.frsa_bwd(ctypes.byref(a), None) == 1              # no d_o / dq / dk / dv
     big = _args(N=257, n_pos=256, d_o=0x1000, dq=0x1000, dk=0x1000, dv=0x1000)
     # ABI 2: S = min(T, 8) partial slots of B*H*N*D floats (T = 3 key tiles here),
-    # counters ((B*H*T*(1 + S) + 4) & ~3 int32) and Delta rows (B*H*N floats, only
-    # without a caller `delta`).
+    # counters ((B*H*T*(1 + S) + 4) & ~3 int32), the rotated Q and K (16-bit) and
+    # Delta rows (B*H*N floats, only without a caller `delta`).
     T = S = 3
     counters = ((1 * 1 * T * (1 + S) + 4) & ~3) * 4
-    part = S * 257 * 64 * 4
+    part = S * 257 * 64 * 4 + 2 * 257 * 64 * 2        # + rotated Q and K (bf16)
     assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == part + counters + 257 * 4
     big.delta = 0x2000
     assert lib.frsa_bwd_workspace_bytes(ctypes.byref(big)) == part + counters

@@ -55,8 +55,8 @@ def test_block_matches_fp32_reference(dim, heads, side, has_cls):
 
 @pytest.mark.parametrize("dim,heads,side,has_cls", [(768, 12, 14, True), (384, 6, 7, False)])
 def test_fused_qkv_rope_block_matches_unfused(dim, heads, side, has_cls):
-    """RoPE in the QKV-projection epilogue (frsa_qkv_rope) + attention with
-    identity tables, against the same block on the unfused path (same weights):
+    """RoPE in the QKV-projection epilogue (frsa_qkv_rope) + attention without
+    rotation (rope=False), against the same block on the unfused path (same weights):
     output and the gradients of x, W_qkv and b_qkv."""
     from triton_fused_rope_flash_attn_b200.block import RopeAttention
     torch.manual_seed(1)

@@ -267,3 +267,64 @@ def test_tf32_backward_against_oracle(side, has_cls, D):
         assert got.dtype == torch.float32
         err = np.abs(got.double().cpu().numpy() - ref).max() / np.abs(ref).max()
         assert err < 5e-3, (name, err)
+
+
+@pytest.mark.parametrize("B,H,side,has_cls,D,dtype", [(2, 4, 14, True, 64, torch.bfloat16),
+                                                      (1, 3, 24, False, 64, torch.bfloat16),
+                                                      (1, 2, 7, True, 80, torch.float16)])
+def test_strided_qkv_views_read_in_place(B, H, side, has_cls, D, dtype):
+    """q, k, v as the [B, H, N, D] views of a [B, N, 3, H, D] projection output
+    (the ViT block's layout; the reference accepts any strides, fa_rope_full
+    .py:1043) are read through strided tensor maps: outputs and gradients are
+    bitwise equal to those of contiguous copies."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, sdpa_triton_fa_rope
+    N = side * side + int(has_cls)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    qkv = torch.randn(B, N, 3, H, D, device="cuda", generator=g).to(dtype)
+    do = torch.randn(B, H, N, D, device="cuda", generator=g).to(dtype)
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    views = [x.detach().requires_grad_(True) for x in qkv.permute(2, 0, 3, 1, 4).unbind(0)]
+    assert not views[0].is_contiguous()
+    conts = [t.detach().contiguous().requires_grad_(True) for t in views]
+    outs = []
+    for q, k, v in (views, conts):
+        o = sdpa_triton_fa_rope(q, k, v, cs, has_cls=has_cls, H_img=side)
+        o.backward(do)
+        outs.append((o.detach(), q.grad, k.grad, v.grad))
+    for name, a, b in zip(("o", "dq", "dk", "dv"), *outs):
+        assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("B,H,side,has_cls,D", [(2, 3, 14, True, 64), (1, 2, 24, False, 64),
+                                                (1, 2, 7, True, 80)])
+def test_no_rope_flag_equals_identity_tables(B, H, side, has_cls, D):
+    """rope=False (FRSA_FLAG_NO_ROPE: q, k arrive rotated, nothing is rotated,
+    gradients w.r.t. the given q, k) is bitwise the attention with identity
+    tables, and matches the float64 oracle with identity tables."""
+    from triton_fused_rope_flash_attn_b200 import sdpa_triton_fa_rope
+
+    class Identity:
+        def __init__(self, n_pos):
+            self.c = torch.ones(n_pos, D // 2, device="cuda")
+            self.s = torch.zeros(n_pos, D // 2, device="cuda")
+
+        def tables(self):
+            return self.c, self.s
+
+    N = side * side + int(has_cls)
+    q, k, v, do = (t.cuda().bfloat16() for t in seeded_inputs(B, H, N, D, seed=9))
+    outs = []
+    for rope, cs in ((True, Identity(side * side)), (False, None)):
+        qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = sdpa_triton_fa_rope(qd, kd, vd, cs, has_cls=has_cls, H_img=side, rope=rope)
+        o.backward(do)
+        outs.append((o.detach(), qd.grad, kd.grad, vd.grad))
+    for name, a, b in zip(("o", "dq", "dk", "dv"), *outs):
+        assert torch.equal(a, b), name
+    ident = np.ones((side * side, D // 2), np.float32), np.zeros((side * side, D // 2), np.float32)
+    qn, kn, vn, don = (t.double().cpu().numpy() for t in (q, k, v, do))
+    refs = (attn_fwd_np(qn, kn, vn, *ident, has_cls)[0],) + attn_bwd_np(qn, kn, vn, don, *ident,
+                                                                        has_cls)
+    for name, got, ref in zip(("o", "dq", "dk", "dv"), outs[1], refs):
+        mx, mean = err_stats(got.double().cpu().numpy(), ref)
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (name, mx, mean)

@@ -13,6 +13,7 @@ from .build import LIB_PATH
 FRSA_DTYPE_BF16 = 0
 FRSA_DTYPE_F16 = 1
 FRSA_DTYPE_F32 = 2
+FRSA_FLAG_NO_ROPE = 1
 
 EXPORTED_SYMBOLS = (
     "frsa_fwd",
@@ -55,6 +56,10 @@ class FrsaAttnArgs(ctypes.Structure):
         ("io_dtype", ctypes.c_int32),
         ("compute_dtype", ctypes.c_int32),
         ("scale", ctypes.c_float),
+        ("q_strides", ctypes.c_int64 * 3),
+        ("k_strides", ctypes.c_int64 * 3),
+        ("v_strides", ctypes.c_int64 * 3),
+        ("flags", ctypes.c_int32),
     ]
 
 

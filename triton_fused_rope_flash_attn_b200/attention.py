@@ -89,25 +89,45 @@ def _ext():
     return _EXT
 
 
-def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True, scale=None):
-    """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]``, all bf16, f16 or f32.
+_NO_TABLE = {}
+
+
+def _tables_or_placeholder(cosp, sinp, rope, device):
+    if rope:
+        return cosp, sinp
+    if device not in _NO_TABLE:
+        _NO_TABLE[device] = torch.empty(0, device=device, dtype=torch.float32)
+    return _NO_TABLE[device], _NO_TABLE[device]
+
+
+def fused_rope_attention_fwd(q, k, v, cosp, sinp, has_cls: bool = True, scale=None,
+                             rope: bool = True):
+    """Forward through the C ABI. ``q, k, v``: CUDA ``[B, H, N, D]``, all bf16, f16 or f32
+    (any b/h/n strides that are multiples of 16 bytes are read in place).
 
     Returns ``(o, lse)`` with ``lse`` float32 ``[B, H, N]`` (natural log).
-    ``scale`` multiplies the logits (default ``1/sqrt(D)``).
+    ``scale`` multiplies the logits (default ``1/sqrt(D)``). ``rope=False``:
+    q and k are already rotated (the tables are not used and may be None).
     """
-    o, lse, rc = _ext().fwd(q, k, v, cosp, sinp, bool(has_cls), -1.0 if scale is None else scale)
+    cosp, sinp = _tables_or_placeholder(cosp, sinp, rope, q.device)
+    o, lse, rc = _ext().fwd(q, k, v, cosp, sinp, bool(has_cls), -1.0 if scale is None else scale,
+                            0 if rope else _lib.FRSA_FLAG_NO_ROPE)
     _lib.check(rc, "frsa_fwd")
     return o, lse
 
 
 def fused_rope_attention_bwd(q, k, v, o, lse, d_o, cosp, sinp, has_cls: bool = True,
-                             delta_out=None, scale=None):
+                             delta_out=None, scale=None, rope: bool = True):
     """Backward through the C ABI. Returns ``(dq, dk, dv)`` in ``q.dtype``.
 
     ``delta_out`` (optional float32 ``[B, H, N]``) receives ``rowsum(dO * O)``.
+    ``rope=False``: q and k are already rotated and dq, dk are the gradients
+    with respect to them.
     """
+    cosp, sinp = _tables_or_placeholder(cosp, sinp, rope, q.device)
     dq, dk, dv, rc = _ext().bwd(q, k, v, o, lse, d_o, cosp, sinp, bool(has_cls), delta_out,
-                                -1.0 if scale is None else scale)
+                                -1.0 if scale is None else scale,
+                                0 if rope else _lib.FRSA_FLAG_NO_ROPE)
     _lib.check(rc, "frsa_bwd")
     return dq, dk, dv
 
@@ -132,22 +152,23 @@ def _pow2_normaliser(x: torch.Tensor, target: float = 1.0) -> float:
 # largest magnitude to 1 (dO to 1/8, leaving headroom for dV = P^T dO and
 # dQ = dS K), the logit scale absorbs the Q and K factors, and the gradients
 # are divided back and returned in fp32.
-def _fp32_forward(Q, K, V, COSP, SINP, has_cls):
+def _fp32_forward(Q, K, V, COSP, SINP, has_cls, rope=True):
     return fused_rope_attention_fwd(Q.contiguous(), K.contiguous(), V.contiguous(), COSP, SINP,
-                                    has_cls)
+                                    has_cls, rope=rope)
 
 
-def _fp32_backward(Q, K, V, O, lse, dO, COSP, SINP, has_cls):
+def _fp32_backward(Q, K, V, O, lse, dO, COSP, SINP, has_cls, rope=True):
     D = Q.shape[-1]
     if D <= 64:
-        return fused_rope_attention_bwd(Q, K, V, O, lse, dO.contiguous(), COSP, SINP, has_cls)
+        return fused_rope_attention_bwd(Q, K, V, O, lse, dO.contiguous(), COSP, SINP, has_cls,
+                                        rope=rope)
     sq, sk, sv = _pow2_normaliser(Q), _pow2_normaliser(K), _pow2_normaliser(V)
     sd = _pow2_normaliser(dO, 0.125)
     qh, kh, vh = (Q * sq).half(), (K * sk).half(), (V * sv).half()
     oh, doh = (O * sv).half(), (dO * sd).half()
     scale = 1.0 / math.sqrt(D) / (sq * sk)
     dq, dk, dv = fused_rope_attention_bwd(qh, kh, vh, oh, lse, doh, COSP, SINP, has_cls,
-                                          scale=scale)
+                                          scale=scale, rope=rope)
     dq = dq.float() * (sq / (sd * sv))
     dk = dk.float() * (sk / (sd * sv))
     dv = dv.float() / sd
@@ -161,7 +182,7 @@ class TritonAttention(torch.autograd.Function):
     """Fused 2D-RoPE SDPA with the reference's autograd contract (fa_rope_full .py:1011-1138)."""
 
     @staticmethod
-    def forward(ctx, Q, K, V, cos_sin, H_img=14, has_cls=True):
+    def forward(ctx, Q, K, V, cos_sin, H_img=14, has_cls=True, rope=True):
         BATCH_SIZE, NUM_HEADS, SEQ_LEN, HEAD_DIM = Q.size()
         assert (HEAD_DIM % 4) == 0, "HEAD_DIM must be divisible by 4 (2D RoPE requires pairs)."
         N_img = H_img ** 2
@@ -174,18 +195,22 @@ class TritonAttention(torch.autograd.Function):
         comp = _sdpa_comp_dtype(Q)
         if not Q.is_cuda:
             raise RuntimeError("sdpa_triton_fa_rope needs CUDA tensors (there is no CPU path)")
-        COSP, SINP = cos_sin.tables()
-        _check_tables(COSP, SINP, SEQ_LEN, HEAD_DIM, has_cls, Q.device)
+        if rope:
+            COSP, SINP = cos_sin.tables()
+            _check_tables(COSP, SINP, SEQ_LEN, HEAD_DIM, has_cls, Q.device)
+        else:   # q and k arrive rotated: no tables
+            COSP, SINP = _tables_or_placeholder(None, None, False, Q.device)
         ctx.comp = comp
         ctx.has_cls = has_cls
+        ctx.rope = rope
         ctx.io_dtypes = (Q.dtype, K.dtype, V.dtype)
         if comp == torch.float32:
             Qf, Kf, Vf = (t.float().contiguous() for t in (Q, K, V))
-            o, lse = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls)
+            o, lse = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls, rope)
             ctx.save_for_backward(Qf, Kf, Vf, o, lse, COSP, SINP)
             return o.to(Q.dtype)
         qc, kc, vc = (t.to(comp) for t in (Q, K, V))
-        o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls)
+        o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls, rope=rope)
         ctx.save_for_backward(qc, kc, vc, o, lse, COSP, SINP)
         return o.to(Q.dtype)
 
@@ -193,23 +218,28 @@ class TritonAttention(torch.autograd.Function):
     def backward(ctx, dO):
         qc, kc, vc, o, lse, COSP, SINP = ctx.saved_tensors
         if ctx.comp == torch.float32:
-            dq, dk, dv = _fp32_backward(qc, kc, vc, o, lse, dO.float(), COSP, SINP, ctx.has_cls)
+            dq, dk, dv = _fp32_backward(qc, kc, vc, o, lse, dO.float(), COSP, SINP, ctx.has_cls,
+                                        ctx.rope)
         else:
             dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
-                                                  ctx.has_cls)
+                                                  ctx.has_cls, rope=ctx.rope)
         qd, kd, vd = ctx.io_dtypes
-        return dq.to(qd), dk.to(kd), dv.to(vd), None, None, None
+        return dq.to(qd), dk.to(kd), dv.to(vd), None, None, None, None
 
 
 def sdpa_triton_fa_rope(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, cos_sin, *,
-                        has_cls: bool = True, H_img: int | None = None):
+                        has_cls: bool = True, H_img: int | None = None, rope: bool = True):
     """Fused 2D-RoPE SDPA forward; differentiable (fa_rope_full .py:1169-1170).
 
     With the reference's four positional arguments this behaves like the
-    reference. ``has_cls`` and ``H_img`` are keyword extensions; ``H_img``
-    defaults to the side of ``cos_sin``'s table (14 for the reference's 14x14 grid).
+    reference. ``has_cls``, ``H_img`` and ``rope`` are keyword extensions;
+    ``H_img`` defaults to the side of ``cos_sin``'s table (14 for the
+    reference's 14x14 grid). ``rope=False``: Q and K are already rotated (for
+    example by the fused QKV projection), nothing is rotated and the Q/K
+    gradients are with respect to the given tensors; ``cos_sin`` may be None
+    (then ``H_img`` must be given).
     """
     if H_img is None:
         n_pos = cos_sin.tables()[0].shape[0]
         H_img = math.isqrt(n_pos)
-    return TritonAttention.apply(Q, K, V, cos_sin, H_img, has_cls)
+    return TritonAttention.apply(Q, K, V, cos_sin, H_img, has_cls, rope)

@@ -38,16 +38,16 @@ class RopeAttention(nn.Module):
         dev = device if device is not None else "cuda"
         self.rope = CosSinTable(rope_base, H_img, self.head_dim, device=dev)
         # fused_qkv: the projection kernel applies the RoPE in its epilogue and
-        # the attention runs with identity tables.
+        # the attention rotates nothing (rope=False).
         self.fused_qkv = fused_qkv
-        self.identity = _qkv.IdentityTables(H_img * H_img, self.head_dim, dev)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, N, C = x.shape
         if self.fused_qkv and _qkv.supported(C, self.num_heads, x.dtype):
             q, k, v = _qkv.qkv_rope(x, self.qkv.weight, self.qkv.bias, self.rope, self.num_heads,
                                     self.has_cls)
-            o = sdpa_triton_fa_rope(q, k, v, self.identity, has_cls=self.has_cls, H_img=self.H_img)
+            o = sdpa_triton_fa_rope(q, k, v, None, has_cls=self.has_cls, H_img=self.H_img,
+                                    rope=False)
             return self.proj(o.transpose(1, 2).reshape(B, N, C))
         qkv = self.qkv(x).view(B, N, 3, self.num_heads, self.head_dim)
         q, k, v = qkv.permute(2, 0, 3, 1, 4).unbind(0)        # [B, H, N, D] views

@@ -94,30 +94,52 @@ thread_local int g_last_encode_result = 0;
 // Detail of the last FRSA_ERR_LAUNCH on this host thread.
 thread_local char g_last_detail[256] = "";
 
-// 3-D map over a contiguous [BH, N, D] 16-bit tensor: dims {D, N, BH}, box
-// {64, 128, 1}, 128-byte swizzle, zero fill outside the tensor. For float32
-// tensors (s.f32) the box is {32, 128, 1}: 128 bytes per row as well.
-// atom32: for float32 operands read MN-major by kind::tf32 products, the
-// 128-byte swizzle with 32-byte atoms that such operands need.
+// 4-D map over a [B, H, N, D] tensor: dims {D, N, H, B}; `st` gives the
+// n, h, b strides in elements (nullptr: contiguous). Box {64, 128, 1, 1} for
+// 16-bit tensors, {32, 128, 1, 1} for float32 (s.f32): 128 bytes per row
+// either way, 128-byte swizzle, zero fill outside the tensor. atom32: for
+// float32 operands read MN-major by kind::tf32 products, the 128-byte swizzle
+// with 32-byte atoms that such operands need.
 bool encode_map(CUtensorMap* m, const void* base, const frsa::LaunchShape& s,
-                bool atom32 = false) {
+                bool atom32 = false, const int64_t* st = nullptr) {
   auto fn = get_encode_fn();
   if (!fn) return false;
   const cuuint64_t elt = s.f32 ? 4 : 2;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(s.D), static_cast<cuuint64_t>(s.N),
-                              static_cast<cuuint64_t>(s.BH)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.D) * elt,
-                                 static_cast<cuuint64_t>(s.D) * s.N * elt};
-  const cuuint32_t box[3] = {s.f32 ? 32u : 64u, 128, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
+  const cuuint64_t H = static_cast<cuuint64_t>(s.H), B = static_cast<cuuint64_t>(s.BH / s.H);
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(s.D), static_cast<cuuint64_t>(s.N), H, B};
+  const cuuint64_t sn = st ? static_cast<cuuint64_t>(st[2]) : static_cast<cuuint64_t>(s.D);
+  const cuuint64_t sh = st ? static_cast<cuuint64_t>(st[1]) : sn * s.N;
+  const cuuint64_t sb = st ? static_cast<cuuint64_t>(st[0]) : sh * H;
+  const cuuint64_t strides[3] = {sn * elt, sh * elt, sb * elt};
+  const cuuint32_t box[4] = {s.f32 ? 32u : 64u, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt = s.f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : s.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const CUresult r = fn(m, dt,
-                        3, const_cast<void*>(base), dims, strides, box, estr,
+                        4, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
+  return r == CUDA_SUCCESS;
+}
+
+// 3-D f32 map {D, N, planes} over contiguous [planes, N, D] rows, box
+// {32, 128, 1}, 128-byte swizzle (the general backward's partial-dQ slots).
+bool encode_map_f32_3d(CUtensorMap* m, const float* base, long long planes, int N, int D) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N),
+                              static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 4,
+                                 static_cast<cuuint64_t>(D) * N * 4};
+  const cuuint32_t box[3] = {32, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) g_last_encode_result = static_cast<int>(r);
   return r == CUDA_SUCCESS;
 }
@@ -151,13 +173,15 @@ int launch_error(const char* where, cudaError_t e) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Caller strides of a q/k/v tensor, or nullptr when it is contiguous.
+const int64_t* strides_of(const int64_t* st) {
+  return (st[0] == 0 && st[1] == 0 && st[2] == 0) ? nullptr : st;
+}
+
 // f32 map {D, N, nslot * BH} over the general backward's partial-dQ slots,
 // box {32, 128, 1}, 128-byte swizzle.
 bool encode_part_map(CUtensorMap* m, const float* part, const frsa::LaunchShape& s, int nslot) {
-  frsa::LaunchShape p = s;
-  p.f32 = true;
-  p.BH = s.BH * nslot;
-  return encode_map(m, part, p);
+  return encode_map_f32_3d(m, part, static_cast<long long>(s.BH) * nslot, s.N, s.D);
 }
 
 // A CUDA error already pending on this host thread (left by the caller's own
@@ -174,11 +198,13 @@ int pending_error(const char* where) {
 
 int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   if (!a) return FRSA_ERR_NULL_ARG;
-  if (!a->q || !a->k || !a->v || !a->cosp || !a->sinp) return FRSA_ERR_NULL_ARG;
+  const bool rope = (a->flags & FRSA_FLAG_NO_ROPE) == 0;
+  if (a->flags & ~FRSA_FLAG_NO_ROPE) return FRSA_ERR_BAD_SHAPE;
+  if (!a->q || !a->k || !a->v || (rope && (!a->cosp || !a->sinp))) return FRSA_ERR_NULL_ARG;
   if (a->B < 1 || a->H < 1 || a->N < 1 || a->D < 1) return FRSA_ERR_BAD_SHAPE;
   if (a->has_cls != 0 && a->has_cls != 1) return FRSA_ERR_BAD_SHAPE;
   if (a->D % 8 != 0 || a->D > 128) return FRSA_ERR_UNSUPPORTED_D;
-  if (a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;  // table must cover every token
+  if (rope && a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;  // table must cover every token
   const long long BH = static_cast<long long>(a->B) * a->H;
   const long long nqt = (a->N + kTile - 1) / kTile;
   if (BH * nqt > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
@@ -186,13 +212,21 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
   if (a->compute_dtype != FRSA_DTYPE_BF16 && a->compute_dtype != FRSA_DTYPE_F16 &&
       a->compute_dtype != FRSA_DTYPE_F32)
     return FRSA_ERR_UNSUPPORTED_DTYPE;
-  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->cosp) ||
-      !aligned16(a->sinp))
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) ||
+      (rope && (!aligned16(a->cosp) || !aligned16(a->sinp))))
     return FRSA_ERR_MISALIGNED;
+  const int64_t elt = a->compute_dtype == FRSA_DTYPE_F32 ? 4 : 2;
+  for (const int64_t* st : {a->q_strides, a->k_strides, a->v_strides}) {
+    if (st[0] == 0 && st[1] == 0 && st[2] == 0) continue;
+    for (int d = 0; d < 3; ++d)
+      if (st[d] < 1 || (st[d] * elt) % 16 != 0 || st[d] * elt >= (int64_t(1) << 40))
+        return FRSA_ERR_MISALIGNED;
+  }
   s->BH = static_cast<int>(BH);
+  s->H = static_cast<int>(a->H);
   s->N = static_cast<int>(a->N);
   s->D = static_cast<int>(a->D);
-  s->has_cls = a->has_cls;
+  s->has_cls = rope ? a->has_cls : -1;   // < 0: the kernels rotate nothing
   s->scale = a->scale;
   s->bf16 = a->compute_dtype == FRSA_DTYPE_BF16;
   s->f32 = a->compute_dtype == FRSA_DTYPE_F32;
@@ -201,12 +235,13 @@ int validate_common(const frsa_attn_args* a, frsa::LaunchShape* s) {
 
 // Workspace of the general 16-bit backward: the f32 partial dQ sums (S slots
 // of BH*N*D floats, S = min(key tiles, 8)), the counters and claim ticket,
-// and, unless the caller passes `delta`, the Delta rows (BH*N floats).
+// the rotated Q and K (BH*N*D 16-bit values each) and, unless the caller
+// passes `delta`, the Delta rows (BH*N floats).
 size_t general_bwd_workspace_bytes(const frsa::LaunchShape& s, bool caller_delta) {
   const size_t rows = static_cast<size_t>(s.BH) * s.N;
   const int S = frsa::bwd_slots(s);
   return S * rows * s.D * sizeof(float) + frsa::bwd_counter_ints(s, S) * sizeof(int) +
-         (caller_delta ? 0 : rows * sizeof(float));
+         2 * rows * s.D * 2 + (caller_delta ? 0 : rows * sizeof(float));
 }
 
 // float32 backward (TF32 tensor cores), D <= 64.
@@ -226,9 +261,11 @@ int bwd_f32(const frsa_attn_args* a, const frsa::LaunchShape& s, void* stream) {
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
   if (const int rc = pending_error("frsa_bwd"); rc != FRSA_OK) return rc;
   CUtensorMap maps[7];   // q16, q32, k16, k32, v16, do16, do32
-  if (!encode_map(&maps[0], a->q, s) || !encode_map(&maps[1], a->q, s, true) ||
-      !encode_map(&maps[2], a->k, s) || !encode_map(&maps[3], a->k, s, true) ||
-      !encode_map(&maps[4], a->v, s) || !encode_map(&maps[5], a->d_o, s) ||
+  const int64_t *sq = strides_of(a->q_strides), *sk = strides_of(a->k_strides),
+                *sv = strides_of(a->v_strides);
+  if (!encode_map(&maps[0], a->q, s, false, sq) || !encode_map(&maps[1], a->q, s, true, sq) ||
+      !encode_map(&maps[2], a->k, s, false, sk) || !encode_map(&maps[3], a->k, s, true, sk) ||
+      !encode_map(&maps[4], a->v, s, false, sv) || !encode_map(&maps[5], a->d_o, s) ||
       !encode_map(&maps[6], a->d_o, s, true))
     return launch_error("frsa_bwd", cudaSuccess);
   const cudaError_t e = frsa::launch_bwd_tf32(
@@ -282,8 +319,10 @@ int frsa_fwd(const frsa_attn_args* a, void* stream) {
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
   if ((rc = pending_error("frsa_fwd")) != FRSA_OK) return rc;
   CUtensorMap tq, tk, tv, to;
-  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) ||
-      !encode_map(&tv, a->v, s, /*atom32=*/s.f32) || !encode_map(&to, a->o, s))
+  if (!encode_map(&tq, a->q, s, false, strides_of(a->q_strides)) ||
+      !encode_map(&tk, a->k, s, false, strides_of(a->k_strides)) ||
+      !encode_map(&tv, a->v, s, /*atom32=*/s.f32, strides_of(a->v_strides)) ||
+      !encode_map(&to, a->o, s))
     return launch_error("frsa_fwd", cudaSuccess);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t e =
@@ -313,7 +352,9 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
   if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
   if ((rc = pending_error("frsa_bwd")) != FRSA_OK) return rc;
   CUtensorMap tq, tk, tv, tdo, to, tgrads[3];
-  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
+  if (!encode_map(&tq, a->q, s, false, strides_of(a->q_strides)) ||
+      !encode_map(&tk, a->k, s, false, strides_of(a->k_strides)) ||
+      !encode_map(&tv, a->v, s, false, strides_of(a->v_strides)) ||
       !encode_map(&tdo, a->d_o, s) || !encode_map(&to, a->o, s))
     return launch_error("frsa_bwd", cudaSuccess);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -329,15 +370,31 @@ int frsa_bwd(const frsa_attn_args* a, void* stream) {
     const int S = frsa::bwd_slots(s);
     float* part = static_cast<float*>(a->workspace);
     int* counters = reinterpret_cast<int*>(part + S * rows * s.D);
-    float* delta_rows = a->delta ? a->delta
-                                 : reinterpret_cast<float*>(counters + frsa::bwd_counter_ints(s, S));
+    uint16_t* q_rot = reinterpret_cast<uint16_t*>(counters + frsa::bwd_counter_ints(s, S));
+    uint16_t* k_rot = q_rot + rows * s.D;
+    float* delta_rows = a->delta ? a->delta : reinterpret_cast<float*>(k_rot + rows * s.D);
+    frsa::QkRotation rot;
+    rot.q = a->q;
+    rot.k = a->k;
+    const int64_t* sq = strides_of(a->q_strides);
+    const int64_t* sk = strides_of(a->k_strides);
+    const long long cn = s.D, ch = static_cast<long long>(s.D) * s.N,
+                    cb = static_cast<long long>(s.D) * s.N * s.H;
+    for (int d = 0; d < 3; ++d) {
+      const long long dflt = d == 0 ? cb : d == 1 ? ch : cn;
+      rot.q_strides[d] = sq ? sq[d] : dflt;
+      rot.k_strides[d] = sk ? sk[d] : dflt;
+    }
+    rot.q_rot = q_rot;
+    rot.k_rot = k_rot;
     CUtensorMap tpart;
-    if (!encode_map(&tgrads[1], a->dk, s) || !encode_map(&tgrads[2], a->dv, s) ||
+    if (!encode_map(&tq, q_rot, s) || !encode_map(&tk, k_rot, s) ||
+        !encode_map(&tgrads[1], a->dk, s) || !encode_map(&tgrads[2], a->dv, s) ||
         !encode_part_map(&tpart, part, s, S))
       return launch_error("frsa_bwd", cudaSuccess);
     e = frsa::launch_bwd_ordered(s, tq, tk, tv, tdo, to, tgrads[1], tgrads[2], tpart, a->o, a->d_o,
                                  a->lse, a->delta, a->cosp, a->sinp, a->dq, a->dk, a->dv, part, S,
-                                 counters, delta_rows, st);
+                                 counters, delta_rows, &rot, st);
   }
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd", e);
 }
@@ -378,6 +435,13 @@ int frsa_trace_copy(unsigned long long* host, size_t n) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FRSA_ERR_LAUNCH;
   return cudaMemcpyFromSymbol(host, frsa::g_trace, n * sizeof(unsigned long long)) ==
                  cudaSuccess ? FRSA_OK : FRSA_ERR_LAUNCH;
+}
+int frsa_trace_copy_it(unsigned long long* ts, unsigned int* fl, size_t n) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return FRSA_ERR_LAUNCH;
+  if (cudaMemcpyFromSymbol(ts, frsa::g_trace_it, n * sizeof(unsigned long long)) != cudaSuccess)
+    return FRSA_ERR_LAUNCH;
+  return cudaMemcpyFromSymbol(fl, frsa::g_trace_fl, n * sizeof(unsigned int)) == cudaSuccess
+             ? FRSA_OK : FRSA_ERR_LAUNCH;
 }
 #endif
 

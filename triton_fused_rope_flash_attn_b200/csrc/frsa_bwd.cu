@@ -98,8 +98,10 @@ struct BwdSmem {
   uint64_t q_full[QS], q_empty[QS];
   uint64_t kq_ready, st_full, st_free, ds_full, mm_done, dq_free, acc_free;
   uint64_t unit_full[kUnitRing], unit_empty[kUnitRing];
+  uint64_t stage_full, stage_free;   // result jobs: row warps -> store warps
+  int job_type, job_bh, job_j, job_i;
+  int red_flag, red_bh, red_i;       // store warps -> row warps: a query tile to complete
   int unit[kUnitRing];
-  int last_arrival;            // broadcast: this CTA completes the dQ of the query tile
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -121,10 +123,97 @@ struct BwdParams {
   int* turns;        // [BH * nqt * nslot] slot turn counters, zero at launch
   int* ticket;       // unit claim counter, zero at launch
   int nslot;         // partial slots S (1 .. nkv)
-  int BH, N, D, nqt, nkv, has_cls;
+  int rot_in;        // 1: rotate the Q and K tiles here; 0: they arrive rotated
+  int BH, H, N, D, nqt, nkv, has_cls;
   float c2;     // scale * log2(e)
   float scale;
 };
+
+// Complete query tile i of head bh (run by the 256 row threads; rw0 = the
+// warp's first row): every key tile has added its share, so sum the S slots
+// in slot order, un-rotate with R^T (fa_rope_full .py:974-993), store the dQ
+// rows (quad layout: 8 lanes per 128-byte row segment, all slots' loads
+// issued before the sums), then drop the slots' lines from L2 without a
+// write-back.
+template <typename T, int NCH>
+__device__ __forceinline__ void complete_dq_tile(const BwdParams& prm, int bh, int i, int rw0,
+                                              int lane) {
+  constexpr int RW = kRowsPerWarp;
+  const int N = prm.N, D = prm.D, S = prm.nslot;
+  const size_t head_elems = static_cast<size_t>(N) * D;
+  const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
+  __threadfence();
+  const int rq = lane >> 3, gl = lane & 7;
+  const int q0 = i * kTile;
+  T* dq_head = reinterpret_cast<T*>(prm.dq) + static_cast<size_t>(bh) * head_elems;
+  const float* part0 = prm.dq_part + static_cast<size_t>(bh) * head_elems;
+  // QB of the warp's quads of rows are summed together, one slot per round
+  // (2 QB loads in flight per lane): a completion costs S L2 round trips per
+  // group of quads and 64-column chunk.
+  constexpr int KQ = RW / 4;               // quads per warp
+  constexpr int QB = (NCH == 1) ? KQ : 2;  // quads per round
+#pragma unroll 1
+  for (int hk = 0; hk < NCH * (KQ / QB); ++hk) {
+    const int h = hk / (KQ / QB), k0 = (hk - h * (KQ / QB)) * QB;
+    const int gg = gl + 8 * h;
+    if (8 * gg >= D) continue;
+    float v[QB][8];
+    const float4* src[QB];
+    bool ok[QB];
+#pragma unroll
+    for (int k = 0; k < QB; ++k) {
+      const int tk = q0 + rw0 + 4 * (k0 + k) + rq;
+      ok[k] = tk < N;
+      src[k] = reinterpret_cast<const float4*>(part0 + static_cast<size_t>(ok[k] ? tk : 0) * D +
+                                               8 * gg);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
+    }
+#pragma unroll 1
+    for (int sl = 0; sl < S; ++sl) {
+      float4 a[QB], bq[QB];
+#pragma unroll
+      for (int k = 0; k < QB; ++k)
+        if (ok[k]) {
+          a[k] = __ldcg(src[k] + sl * (slot_stride / 4));
+          bq[k] = __ldcg(src[k] + sl * (slot_stride / 4) + 1);
+        }
+#pragma unroll
+      for (int k = 0; k < QB; ++k)
+        if (ok[k]) {
+          // slot order: v starts at 0, and 0 + x == x
+          v[k][0] += a[k].x; v[k][1] += a[k].y; v[k][2] += a[k].z; v[k][3] += a[k].w;
+          v[k][4] += bq[k].x; v[k][5] += bq[k].y; v[k][6] += bq[k].z; v[k][7] += bq[k].w;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < QB; ++k) {
+      const int tk = q0 + rw0 + 4 * (k0 + k) + rq;
+      if (!ok[k]) continue;
+      const int p2 = rope_pos(tk, N, prm.has_cls);
+      if (p2 >= 0) {
+        const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
+        unrotate8(v[k], __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
+                  __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gg));
+      }
+      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) = pack8<T>(v[k]);
+    }
+  }
+  named_bar(1, kComputeThreads);
+  // Only lines wholly inside this tile's rows: a line shared with a
+  // neighbouring tile or head may still be live.
+  const int q_rows = min(kTile, N - q0);
+  const int tid = threadIdx.x - 128;
+  for (int sl = 0; sl < S; ++sl) {
+    const uintptr_t lo =
+        reinterpret_cast<uintptr_t>(part0 + sl * slot_stride + static_cast<size_t>(q0) * D);
+    const uintptr_t hi = lo + static_cast<uintptr_t>(q_rows) * D * 4;
+    const uintptr_t l0 = (lo + 127) & ~static_cast<uintptr_t>(127);
+    for (uintptr_t ln = l0 + 128 * static_cast<uintptr_t>(tid); ln + 128 <= hi;
+         ln += 128 * kComputeThreads)
+      discard_l2_line(reinterpret_cast<const void*>(ln));
+  }
+}
 
 template <typename T, int NCH>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -167,6 +256,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&sm.st_free, 1);
     mbar_init(&sm.dq_free, 1);
     mbar_init(&sm.acc_free, 1);
+    mbar_init(&sm.stage_full, 1);
+    mbar_init(&sm.stage_free, 1);
     for (int s = 0; s < kUnitRing; ++s) {
       mbar_init(&sm.unit_full[s], 1);
       mbar_init(&sm.unit_empty[s], 1 + kComputeThreads);
@@ -177,7 +268,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tmem_alloc(&sm.tmem_base, kTmemColsBwd);
     tmem_relinquish();
   }
-  FRSA_STAMP(31);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -220,20 +310,88 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_wait(&sm.kv_empty[ks], ((n / KVS) & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.kv_full[ks], 2 * NCH * kChunkBytes);
         for (int c = 0; c < NCH; ++c) {
-          tma_load_3d(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
-          tma_load_3d(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh);
+          tma_load_bh(sm.k[ks][c], &tm_k, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh, prm.H);
+          tma_load_bh(sm.v[ks][c], &tm_v, &sm.kv_full[ks], c * kChunkCols, j * kTile, bh, prm.H);
         }
         for (int i = 0; i < nqt; ++i, ++qi) {
           const int qs = qi % QS;
           mbar_wait(&sm.q_empty[qs], ((qi / QS) & 1) ^ 1, abort_flag);
           mbar_arrive_expect_tx(&sm.q_full[qs], 2 * NCH * kChunkBytes);
           for (int c = 0; c < NCH; ++c) {
-            tma_load_3d(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
-            tma_load_3d(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh);
+            tma_load_bh(sm.q[qs][c], &tm_q, &sm.q_full[qs], c * kChunkCols, i * kTile, bh, prm.H);
+            tma_load_bh(sm.dO[qs][c], &tm_do, &sm.q_full[qs], c * kChunkCols, i * kTile, bh, prm.H);
+            // The tile after it into L2 now: its load is issued only when a
+            // stage frees, and then mostly hits L2.
+            if (i + 1 < nqt) {
+              tma_prefetch_l2_bh(&tm_q, c * kChunkCols, (i + 1) * kTile, bh, prm.H);
+              tma_prefetch_l2_bh(&tm_do, c * kChunkCols, (i + 1) * kTile, bh, prm.H);
+            }
           }
         }
       }
     }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ store warps
+    // Warps 2 and 3 take finished result tiles from the stage (jobs posted by
+    // the row warps) and write them with TMA stores issued by lane 0 of warp
+    // 2: dV/dK tiles, and dQ^ shares into their partial slot (a plain store
+    // for the first key tile of the slot, else an L2 reduce-add after that
+    // slot's turn). Once a share is in L2 the slot's next turn is released and
+    // the key tile counted in on the (head, query tile) arrival counter; when
+    // it arrived last, the row warps are told (with the stage's release) to
+    // complete that query tile's dQ. Nothing here waits on the row warps
+    // beyond the job hand-off.
+    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
+    const int S = prm.nslot;
+    const bool issuer = threadIdx.x == 64;
+    const size_t head_elems = static_cast<size_t>(N) * D;
+    const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
+    for (int m = 0;; ++m) {
+      mbar_wait(&sm.stage_full, m & 1, abort_flag);
+      const int type = *abort_flag ? 0 : *reinterpret_cast<volatile int*>(&sm.job_type);
+      const int bh = sm.job_bh, j = sm.job_j, i = sm.job_i;
+      if (type == 0) break;    // no more jobs
+      if (issuer) {
+        bool last = false;
+        if (type == 1) {
+          // dV chunk c at stage chunk c, dK chunk c at stage chunk NCH + c.
+          for (int c = 0; c < NCH; ++c) {
+            if (c * 64 < D) {
+              tma_store_bh(&tm_dv, stage + c * kChunkBytes, c * kChunkCols, j * kTile, bh, prm.H);
+              tma_store_bh(&tm_dk, stage + (NCH + c) * kChunkBytes, c * kChunkCols, j * kTile, bh,
+                           prm.H);
+            }
+          }
+          tma_store_commit();
+          tma_store_wait_read();
+          sm.red_flag = 0;
+          mbar_arrive(&sm.stage_free);
+        } else {
+          const int slot = j % S, gen = j / S;
+          if (gen > 0)
+            flag_wait_geq(prm.turns + (static_cast<size_t>(bh) * nqt + i) * S + slot, gen,
+                          abort_flag);
+          const int z = slot * prm.BH + bh;
+          for (int h = 0; 32 * h < D; ++h) {
+            if (gen > 0) tma_reduce_add_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i * kTile, z);
+            else tma_store_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i * kTile, z);
+          }
+          tma_store_commit();
+          tma_store_wait_all();   // the share is in L2 (and the stage read)
+          __threadfence();
+          if (j + S < prm.nkv) st_release_gpu(prm.turns + (static_cast<size_t>(bh) * nqt + i) * S +
+                                                  slot, gen + 1);
+          last = atomicAdd(prm.arrive + static_cast<size_t>(bh) * nqt + i, 1) == prm.nkv - 1;
+          // The key tile arriving last completes the query tile: the row
+          // warps pick this up when they next acquire the stage.
+          sm.red_flag = last ? 1 : 0;
+          sm.red_bh = bh;
+          sm.red_i = i;
+          mbar_arrive(&sm.stage_free);
+        }
+      }
+    }
+    if (issuer) tma_store_wait_all();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -308,13 +466,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             u2 = next_unit(n2);
           }
           const bool more = u2 >= 0;
-          if (kAhead && more) {
-            mbar_wait(&sm.st_free, t & 1, abort_flag);       // S^T/dP^T of t in registers
-            tc_fence_after();
-            issue_st(n2, i2, t + 1);
-          }
           issue_grads(n, i, t, j);
-          if (!kAhead && more) {
+          if (more) {
             mbar_wait(&sm.st_free, t & 1, abort_flag);
             tc_fence_after();
             issue_st(n2, i2, t + 1);
@@ -349,26 +502,39 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
     // Rotate the key tile of the n_-th unit (key tile j_) in its stage.
     auto prep_k = [&](int j_, int n_) {
-      RopeQ<NCH, RW> rope;
-      load_rope_q<NCH, RW>(rope, rw0, j_ * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.kv_full[n_ % KVS], (n_ / KVS) & 1, abort_flag);
-      apply_rope_q<T, NCH, RW>(&sm.k[n_ % KVS][0][0], rw0, D, rope, lane);
+      if (prm.rot_in) {
+        RopeQ<NCH, RW> rope;
+        load_rope_q<NCH, RW>(rope, rw0, j_ * kTile, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        mbar_wait(&sm.kv_full[n_ % KVS], (n_ / KVS) & 1, abort_flag);
+        if (prm.has_cls >= 0) apply_rope_q<T, NCH, RW>(&sm.k[n_ % KVS][0][0], rw0, D, rope, lane);
+      } else {
+        mbar_wait(&sm.kv_full[n_ % KVS], (n_ / KVS) & 1, abort_flag);
+      }
     };
     // Prepare query tile i_ of head bh_ (key tile j_) in stage t_ % QS
     // (iteration t_): lse2 (+inf for padded rows, so their P is exactly 0),
     // rotation of Q, and Delta; then tell the MMA warp.
-    auto prep_q = [&](int bh_, int j_, int i_, int t_) {
+    // lse2 (+inf for padded rows) and Delta (when precomputed) of query row r
+    // of tile i_ of head bh_, for warpgroup 0's threads; loaded an iteration
+    // ahead of their use so their global latency is hidden.
+    // (The raw lse is kept until use, so nothing waits on these loads early.)
+    auto load_rowstats = [&](int bh_, int i_, float& l2, float& dl) {
+      const size_t row = static_cast<size_t>(bh_) * N + i_ * kTile + r;
+      const bool qv = (i_ * kTile + r) < N;
+      l2 = qv ? __ldg(prm.lse + row) : INFINITY;
+      dl = (qv && prm.delta_in != nullptr) ? __ldg(prm.delta_in + row) : 0.f;
+    };
+    auto prep_q = [&](int bh_, int j_, int i_, int t_, float l2, float dl) {
       const int qs_ = t_ % QS;
       const size_t row0 = static_cast<size_t>(bh_) * N;
       const int q0_ = i_ * kTile;
+      const bool dpre = prm.delta_in != nullptr;
       if (g == 0) {
-        const bool qv = (q0_ + r) < N;
-        sm.lse2[qs_][r] = qv ? prm.lse[row0 + q0_ + r] * 1.4426950408889634f : INFINITY;
+        sm.lse2[qs_][r] = l2 * 1.4426950408889634f;   // +inf stays +inf
+        if (dpre) sm.delta[qs_][r] = dl;
       }
       // O granules of this warp's query rows (quad layout), read before the
       // tile wait so the load overlaps it.
-      const bool dpre = prm.delta_in != nullptr;
-      if (dpre && g == 0) sm.delta[qs_][r] = (q0_ + r) < N ? prm.delta_in[row0 + q0_ + r] : 0.f;
       const int rq = lane >> 3, gl = lane & 7;
       uint4 og[NCH][RW / 4];
 #pragma unroll
@@ -381,10 +547,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                                                 (row0 + tok) * D) + gg)
                          : make_uint4(0u, 0u, 0u, 0u);
         }
-      RopeQ<NCH, RW> rope;
-      load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
-      mbar_wait(&sm.q_full[qs_], (t_ / QS) & 1, abort_flag);
-      apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      if (prm.rot_in) {
+        RopeQ<NCH, RW> rope;
+        load_rope_q<NCH, RW>(rope, rw0, q0_, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+        mbar_wait(&sm.q_full[qs_], (t_ / QS) & 1, abort_flag);
+        if (prm.has_cls >= 0) apply_rope_q<T, NCH, RW>(&sm.q[qs_][0][0], rw0, D, rope, lane);
+      } else {
+        mbar_wait(&sm.q_full[qs_], (t_ / QS) & 1, abort_flag);
+      }
       // Delta = sum_d O dO per query row: each lane dots its granule of O with
       // the same granule of the (unrotated) dO tile; 8 lanes share a row.
       const uint32_t dob = smem_u32(&sm.dO[qs_][0][0]);
@@ -419,103 +589,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (leader) mbar_arrive(&sm.kq_ready);
     };
 
-    // Results of finished iterations leave through shared-memory tiles and
-    // TMA stores issued by the leader thread:
-    //   dV, dK = R^T dK^ scale   bf16 tiles [128 key][64] (128-byte swizzle)
-    //                            -> tm_dv / tm_dk at (64 c, key tile, head)
-    //   dQ^ share * scale        f32 tiles [128 query][32] (128-byte swizzle)
-    //                            -> tm_part at (32 h, query tile, slot * BH + head),
-    //                            a plain store for the first key tile of the
-    //                            slot, else an L2 reduce-add (after its turn).
-    // The share's completion (and its turn release and arrival count) is
-    // collected at the start of the next drain, so the leader does not wait
-    // for its own stores in between.
+    // Results of finished iterations leave through a shared-memory stage: the
+    // row warps fill it (thread = tile row, from TMEM) and post a job to the
+    // store warps, which write it out with TMA stores:
+    //   job 1: dV and dK = R^T dK^ scale of a key tile, bf16 tiles
+    //          [128 key][64] (128-byte swizzle): dV chunk c at stage chunk c,
+    //          dK chunk c at stage chunk NCH + c;
+    //   job 2: a dQ^ share * scale, f32 tiles [128 query][32] (128-byte
+    //          swizzle), 32-column block h at stage chunk h;
+    //   job 0: no more jobs.
     uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
     const uint32_t stb = smem_u32(stage);
-    const int S = prm.nslot;
-    const size_t head_elems = static_cast<size_t>(N) * D;
-    const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
-    int pend_bh = -1, pend_j = 0, pend_i = 0;   // dQ share whose store is in flight
-
-    // Sum the slots of query tile i_ of head bh_ in slot order, un-rotate,
-    // store dQ (quad layout: 8 lanes per 128-byte row segment), then drop the
-    // slots' lines from L2 without a write-back.
-    auto reduce_tile = [&](int bh_, int i_) {
-      __threadfence();
-      const int rq = lane >> 3, gl = lane & 7;
-      const int q0 = i_ * kTile;
-      T* dq_head = reinterpret_cast<T*>(prm.dq) + static_cast<size_t>(bh_) * head_elems;
-      const float* part0 = prm.dq_part + static_cast<size_t>(bh_) * head_elems;
-#pragma unroll
-      for (int k = 0; k < RW / 4; ++k) {
-        const int rr = rw0 + 4 * k + rq, tk = q0 + rr;
-#pragma unroll
-        for (int h = 0; h < NCH; ++h) {
-          const int gg = gl + 8 * h;
-          if (tk < N && 8 * gg < D) {
-            const float4* src =
-                reinterpret_cast<const float4*>(part0 + static_cast<size_t>(tk) * D + 8 * gg);
-            float4 a = __ldcg(src), bq = __ldcg(src + 1);
-            float v[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
-            for (int sl = 1; sl < S; ++sl) {
-              src += slot_stride / 4;
-              a = __ldcg(src);
-              bq = __ldcg(src + 1);
-              v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-              v[4] += bq.x; v[5] += bq.y; v[6] += bq.z; v[7] += bq.w;
-            }
-            const int p2 = rope_pos(tk, N, prm.has_cls);
-            if (p2 >= 0) {
-              const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
-              unrotate8(v, __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
-                        __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gg));
-            }
-            *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) =
-                pack8<T>(v);
-          }
-        }
-      }
-      named_bar(1, kComputeThreads);
-      // Only lines wholly inside this tile's rows: a line shared with a
-      // neighbouring tile or head may still be live.
-      const int q_rows = min(kTile, N - q0);
-      const int tid = threadIdx.x - 128;
-      for (int sl = 0; sl < S; ++sl) {
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(part0 + sl * slot_stride +
-                                                         static_cast<size_t>(q0) * D);
-        const uintptr_t hi = lo + static_cast<uintptr_t>(q_rows) * D * 4;
-        const uintptr_t l0 = (lo + 127) & ~static_cast<uintptr_t>(127);
-        for (uintptr_t ln = l0 + 128 * static_cast<uintptr_t>(tid); ln + 128 <= hi;
-             ln += 128 * kComputeThreads)
-          discard_l2_line(reinterpret_cast<const void*>(ln));
+#ifdef FRSA_TRACE
+    unsigned trace_flags = 0;   // events of the current iteration (bit 0: a dQ tile completed)
+#endif
+    int jobs = 0;   // jobs posted so far
+    int acquired = 0;   // jobs whose stage release has been taken
+    // Wait until the store warps are done with the stage (the last posted
+    // job), and complete the query tile that job finished, if any.
+    // (after_dq: the last posted job may have been a dQ share; a dV/dK job
+    // never completes a query tile.)
+    auto stage_acquire = [&](bool after_dq) {
+      if (jobs == acquired) return;
+      mbar_wait(&sm.stage_free, (jobs - 1) & 1, abort_flag);
+      acquired = jobs;
+      if (after_dq && *reinterpret_cast<volatile int*>(&sm.red_flag) && !*abort_flag) {
+        complete_dq_tile<T, NCH>(prm, sm.red_bh, sm.red_i, rw0, lane);
+#ifdef FRSA_TRACE
+        trace_flags |= 1u;
+#endif
       }
     };
-
-    // Collect the dQ share in flight: once it is in L2, release the slot's
-    // next turn and count this key tile in; the last key tile of the head to
-    // arrive completes the query tile's dQ.
-    auto finish_pending = [&]() {
-      if (pend_bh < 0) return;
-      if (leader) {
-        tma_store_wait_all();
-        __threadfence();
-        const int gen = pend_j / S;
-        if (pend_j + S < prm.nkv)
-          st_release_gpu(prm.turns + (static_cast<size_t>(pend_bh) * nqt + pend_i) * S +
-                             pend_j % S, gen + 1);
-        const int before = atomicAdd(prm.arrive + static_cast<size_t>(pend_bh) * nqt + pend_i, 1);
-        sm.last_arrival = (before == prm.nkv - 1);
-      }
+    auto post = [&](int type, int bh_, int j_, int i_) {
+      fence_proxy_async_smem();
       named_bar(1, kComputeThreads);
-      if (sm.last_arrival) reduce_tile(pend_bh, pend_i);
-      pend_bh = -1;
+      if (leader) {
+        sm.job_type = type;
+        sm.job_bh = bh_;
+        sm.job_j = j_;
+        sm.job_i = i_;
+        mbar_arrive(&sm.stage_full);
+      }
+      ++jobs;
     };
 
     // Results of a finished iteration (its products done, mm_done waited):
     // this key tile's dQ^ share of query tile i_, and at the unit's last
     // query tile the unit's dV and dK^ (thread = tile row for TMEM reads).
-    auto drain = [&](int bh_, int j_, int i_) {
-      finish_pending();   // also: the stage is free (that store has completed)
+    int trace_ts = -1;   // trace builds: stamp slots of the current iteration
+    auto drain = [&](int bh_, int j_, int i_, bool flush) {
       const bool unit_end = (i_ == nqt - 1);
       // kAhead: the MMA warp's next dQ^ product waits for these columns, so
       // they are read out (two 16-column blocks per thread) and released
@@ -523,7 +645,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // drain is over and blocks are read one at a time.
       constexpr int kHeld = kAhead ? kBlk / 2 : 1;
       float qv[kHeld][16];
-      if (kAhead) {
+      if (kAhead && !flush) {
 #pragma unroll
         for (int b = 0; b < kHeld; ++b) {
           const int c16 = g + 2 * b;
@@ -534,9 +656,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         named_bar(1, kComputeThreads);
         if (leader) mbar_arrive(&sm.dq_free);
       }
+      if (trace_ts >= 0) FRSA_STAMP(trace_ts + 6);
+      // (without kAhead the previous dQ job was already taken, and its query
+      // tile completed, before this iteration's P/dS were stored)
+      stage_acquire(kAhead || flush);
+      if (flush) return;
       if (unit_end) {
-        // dV and dK = R^T dK^ scale of key tile j_ as bf16 tiles: dV chunk c
-        // at stage chunk c, dK chunk c at stage chunk NCH + c.
         const int kv0 = j_ * kTile;
         const int pos = rope_pos(kv0 + r, N, prm.has_cls);
 #pragma unroll 1
@@ -567,24 +692,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
         }
-        fence_proxy_async_smem();
         tc_fence_before();
-        named_bar(1, kComputeThreads);
-        if (leader) {
-          mbar_arrive(&sm.acc_free);
-          for (int c = 0; c < NCH; ++c) {
-            if (c * 64 < D) {
-              tma_store_3d(&tm_dv, stage + c * kChunkBytes, c * kChunkCols, kv0, bh_);
-              tma_store_3d(&tm_dk, stage + (NCH + c) * kChunkBytes, c * kChunkCols, kv0, bh_);
-            }
-          }
-          tma_store_commit();
-          tma_store_wait_read();
-        }
-        named_bar(1, kComputeThreads);
+        post(1, bh_, j_, i_);
+        if (leader) mbar_arrive(&sm.acc_free);
+        stage_acquire(false);
       }
-      // dQ^ share * scale -> f32 tiles [128][32]: column block c16 is half
-      // (c16 & 1) of tile c16 >> 1.
 #pragma unroll
       for (int b = 0; b < kBlk / 2; ++b) {
         const int c16 = g + 2 * b;
@@ -604,30 +716,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      named_bar(1, kComputeThreads);
-      if (leader) {
-        if (!kAhead) mbar_arrive(&sm.dq_free);
-        const int slot = j_ % S, gen = j_ / S;
-        if (gen > 0)
-          flag_wait_geq(prm.turns + (static_cast<size_t>(bh_) * nqt + i_) * S + slot, gen,
-                        abort_flag);
-        const int z = slot * prm.BH + bh_;
-        for (int h = 0; 32 * h < D; ++h) {
-          if (gen > 0) tma_reduce_add_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i_ * kTile, z);
-          else tma_store_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i_ * kTile, z);
-        }
-        tma_store_commit();
-        // Without kAhead the stage is the P/dS tiles, rewritten next iteration.
-        if (!kAhead) tma_store_wait_read();
-      }
-      if (!kAhead) named_bar(1, kComputeThreads);
-      pend_bh = bh_;
-      pend_j = j_;
-      pend_i = i_;
+      if (!kAhead) tc_fence_before();
+      post(2, bh_, j_, i_);
+      if (!kAhead && leader) mbar_arrive(&sm.dq_free);
     };
 
+    FRSA_STAMP(56);
     // The iteration sequence, as the MMA warp walks it. With kAhead, an
     // iteration's results are drained during the next iteration (after its
     // P/dS are published); one extra pass drains the last one.
@@ -635,13 +729,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int u = next_unit(0);
     if (u >= 0) {
       int bh = u / prm.nkv, j = u - bh * prm.nkv;
+      float nl2 = 0.f, ndl = 0.f;   // row statistics of the next query tile
+      if (g == 0) load_rowstats(bh, 0, nl2, ndl);
       prep_k(j, n);
-      prep_q(bh, j, 0, 0);
+      prep_q(bh, j, 0, 0, nl2, ndl);
       int pbh = -1, pj = 0, pi = 0, pt = 0;   // iteration waiting to be drained
       bool have = true;                               // iteration t exists
       int n2 = 0, i2 = 0, u2 = -1, bh2 = 0, j2 = 0;
       bool more = false;
       while (true) {
+        const int ts = (t >= 5 && t < 12) ? 8 * (t - 5) : -1;   // trace slots (trace builds)
+        trace_ts = ts;
+#ifdef FRSA_TRACE
+        if (threadIdx.x == FRSA_STAMP_TID && blockIdx.x < 2048 && t < 1024) {
+          g_trace_it[blockIdx.x * 1024 + t] = globaltimer();
+          g_trace_fl[blockIdx.x * 1024 + t] = trace_flags | (static_cast<unsigned>(i) << 8);
+        }
+        trace_flags = 0;
+#endif
+        if (ts >= 0) FRSA_STAMP(ts + 0);
         if (have) {
           n2 = n;
           i2 = i + 1;
@@ -654,15 +760,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           more = u2 >= 0;
           bh2 = more ? u2 / prm.nkv : 0;
           j2 = more ? u2 - bh2 * prm.nkv : 0;
-          if (kAhead && more) {
-            if (n2 != n) prep_k(j2, n2);
-            prep_q(bh2, j2, i2, t + 1);
-          }
+          if (more && g == 0) load_rowstats(bh2, i2, nl2, ndl);
+          if (ts >= 0) FRSA_STAMP(ts + 1);
           // S^T, dP^T of iteration t -> registers; release the TMEM columns.
           const int qs = t % QS;
           const int ncol = 16 * valid16(i);
           mbar_wait(&sm.st_full, t & 1, abort_flag);
           tc_fence_after();
+          if (ts >= 0) FRSA_STAMP(ts + 2);
           // P = exp2(S^T c2 - lse2), dS = P (dP^T - Delta), one 32-column half
           // at a time. Padded query columns have lse2 = +inf (P = 0, dS = 0);
           // padded key rows only reach dV/dK rows that are never stored and dQ
@@ -685,12 +790,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               tc_fence_before();
               named_bar(1, kComputeThreads);
               if (leader) mbar_arrive(&sm.st_free);
+              if (ts >= 0) FRSA_STAMP(ts + 3);
               // P/dS tiles are free once the previous iteration's products
-              // are done (non-kAhead: waited before this iteration began).
+              // are done (non-kAhead: waited before this iteration began, and
+              // the tiles double as the result stage: wait for the store warps).
               if (kAhead && t > 0) {
                 mbar_wait(&sm.mm_done, (t - 1) & 1, abort_flag);
                 tc_fence_after();
               }
+              if (!kAhead) stage_acquire(true);
+              if (ts >= 0) FRSA_STAMP(ts + 4);
               if (64 * g < ncol) {
 #pragma unroll
                 for (int g4 = 0; g4 < 4; ++g4) {
@@ -732,29 +841,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_before();
           named_bar(1, kComputeThreads);
           if (leader) mbar_arrive(&sm.ds_full);
+          if (ts >= 0) FRSA_STAMP(ts + 5);
         }
         // Drain: kAhead the previous iteration (its products finished before
-        // this iteration's P/dS store; on the extra pass wait here), else this one.
-        if (!kAhead) {
+        // this iteration's P/dS store; on the extra pass wait here), else this
+        // one. A last pass with nothing left to drain ("flush") only takes
+        // the stage back, completing the query tile the last job finished.
+        if (!kAhead && have) {
           mbar_wait(&sm.mm_done, t & 1, abort_flag);
           tc_fence_after();
           pbh = bh; pj = j; pi = i; pt = t;
-        } else if (!have && pbh >= 0) {
+        } else if (kAhead && !have && pbh >= 0) {
           mbar_wait(&sm.mm_done, pt & 1, abort_flag);
           tc_fence_after();
         }
-        if (pbh >= 0) drain(pbh, pj, pi);
-        if (!have) break;
-        if (!kAhead && more) {
+        const bool flush = !have && pbh < 0;
+        if (pbh >= 0 || flush) drain(pbh, pj, pi, flush);
+        if (ts >= 0) FRSA_STAMP(ts + 7);
+        if (flush) break;
+        if (!have) {
+          pbh = -1;
+          continue;
+        }
+        // The next query tile: with two stages its load started when the
+        // products of t - 1 finished (waited above), so it has landed by now.
+        if (more) {
           if (n2 != n) prep_k(j2, n2);
-          prep_q(bh2, j2, i2, t + 1);
+          prep_q(bh2, j2, i2, t + 1, nl2, ndl);
         }
         if (kAhead) {
           pbh = bh; pj = j; pi = i; pt = t;
         }
         if (!more) {
-          if (!kAhead) break;
           have = false;
+          if (!kAhead) pbh = -1;
           continue;
         }
         n = n2;
@@ -764,11 +884,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         j = j2;
         ++t;
       }
-      finish_pending();
     }
+    if (u < 0) stage_acquire(false);   // (no work: nothing was posted)
+    post(0, 0, 0, 0);   // no more jobs
+    FRSA_STAMP(57);
+#ifdef FRSA_TRACE
+    if (threadIdx.x == FRSA_STAMP_TID && blockIdx.x < 2048) g_trace[blockIdx.x * 64 + 58] = t + 1;
+#endif
   }
 
-  FRSA_STAMP(30);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -803,6 +927,76 @@ __global__ void delta_rows_kernel(const T* __restrict__ o, const T* __restrict__
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
   if (gl == 0 && row < rows) delta[row] = acc;
+}
+
+// Row pre-pass of the general backward, once per row of [B*H*N, D]: the
+// rotated Q^ = R(Q) and K^ = R(K) (fa_rope_full .py:201-202, 271-272; the same
+// f32 arithmetic and single 16-bit rounding as the in-kernel rotation) into
+// contiguous buffers, and, when `delta` is given, Delta = rowsum(dO * O)
+// (fa_rope_full .py:352-357). Rotating here once, instead of once per (key
+// tile, query tile) inside the main kernel, takes the rotation off its
+// critical path. q and k may be strided ([B, H, N, D], element strides b, h, n).
+// 8 lanes per row, one 16-byte granule each per step.
+struct PrepRows {
+  const void* q;
+  const void* k;
+  const void* o;
+  const void* d_o;
+  long long qs[3], ks[3];   // element strides (b, h, n) of q and k
+  const float* cosp;
+  const float* sinp;
+  void* q_rot;
+  void* k_rot;
+  float* delta;             // nullptr: no Delta
+  long long rows;
+  int N, D, H, has_cls;
+};
+
+template <typename T>
+__global__ void prep_rows_kernel(const PrepRows p) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+  const int gl = threadIdx.x & 7;
+  const bool valid = row < p.rows;
+  const long long bh = valid ? row / p.N : 0;
+  const int n = valid ? static_cast<int>(row - bh * p.N) : 0;
+  const long long b = bh / p.H, h = bh - b * p.H;
+  const int pos = rope_pos(n, p.N, p.has_cls);
+  const T* qrow = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[1] + n * p.qs[2];
+  const T* krow = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[1] + n * p.ks[2];
+  uint4* qdst = reinterpret_cast<uint4*>(static_cast<T*>(p.q_rot) + row * p.D);
+  uint4* kdst = reinterpret_cast<uint4*>(static_cast<T*>(p.k_rot) + row * p.D);
+  float acc = 0.f;
+  for (int gg = gl; 8 * gg < p.D; gg += 8) {
+    if (valid) {
+      float4 c = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (pos >= 0) {
+        const size_t t0 = static_cast<size_t>(pos) * (p.D >> 1);
+        c = __ldg(reinterpret_cast<const float4*>(p.cosp + t0) + gg);
+        sn = __ldg(reinterpret_cast<const float4*>(p.sinp + t0) + gg);
+      }
+      const uint4 xq = __ldg(reinterpret_cast<const uint4*>(qrow) + gg);
+      const uint4 xk = __ldg(reinterpret_cast<const uint4*>(krow) + gg);
+      qdst[gg] = pos >= 0 ? rotate_granule<T>(xq, c, sn) : xq;
+      kdst[gg] = pos >= 0 ? rotate_granule<T>(xk, c, sn) : xk;
+      if (p.delta != nullptr) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.o) + row * p.D) + gg);
+        const uint4 d = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.d_o) + row * p.D) + gg);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x = Elt<T>::unpack(aw[e]), y = Elt<T>::unpack(bw[e]);
+          acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+        }
+      }
+    }
+  }
+  if (p.delta != nullptr) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    if (gl == 0 && valid) p.delta[row] = acc;
+  }
 }
 
 }  // namespace
@@ -854,7 +1048,7 @@ cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
                                const void* d_o, const float* lse, float* delta,
                                const float* cosp, const float* sinp, void* dq, void* dk, void* dv,
                                float* dq_part, int nslot, int* counters, float* delta_buf,
-                               cudaStream_t stream) {
+                               const QkRotation* rot, cudaStream_t stream) {
   const long long rows = static_cast<long long>(s.BH) * s.N;
   BwdParams p;
   p.cosp = cosp;
@@ -868,6 +1062,7 @@ cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
   p.dq_part = dq_part;
   p.nslot = nslot;
   p.BH = s.BH;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
@@ -883,7 +1078,44 @@ cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
   // clearing (the first key tile of each slot stores its share).
   cudaError_t e = cudaMemsetAsync(counters, 0, bwd_counter_ints(s, nslot) * sizeof(int), stream);
   if (e != cudaSuccess) return e;
-  if (delta_buf != nullptr) {
+  p.rot_in = rot == nullptr ? 1 : 0;
+  if (rot != nullptr) {
+    // Q^, K^ (and Delta) once per row here, instead of per (key tile, query
+    // tile) in the main kernel; the caller's maps tm_q / tm_k cover
+    // rot->q_rot / rot->k_rot.
+    PrepRows pr;
+    pr.q = rot->q;
+    pr.k = rot->k;
+    pr.o = o;
+    pr.d_o = d_o;
+    for (int d = 0; d < 3; ++d) {
+      pr.qs[d] = rot->q_strides[d];
+      pr.ks[d] = rot->k_strides[d];
+    }
+    pr.cosp = cosp;
+    pr.sinp = sinp;
+    pr.q_rot = rot->q_rot;
+    pr.k_rot = rot->k_rot;
+    pr.delta = delta_buf;
+    pr.rows = rows;
+    pr.N = s.N;
+    pr.D = s.D;
+    pr.H = s.H;
+    pr.has_cls = s.has_cls;
+    const long long threads_d = rows * 8;
+    if (s.bf16)
+      prep_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0,
+                                        stream>>>(pr);
+    else
+      prep_rows_kernel<__half><<<static_cast<unsigned>((threads_d + 255) / 256), 256, 0,
+                                 stream>>>(pr);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (delta_buf != nullptr) {
+      p.delta_in = delta_buf;
+      p.delta_out = nullptr;   // delta_buf is the caller's delta when one was given
+    }
+  } else if (delta_buf != nullptr) {
     // Delta once per row here, instead of once per (key tile, query tile) in
     // the main kernel (which would also re-read O for every key tile).
     const long long threads_d = rows * 8;

@@ -85,7 +85,7 @@ struct BsParams {
   void* dq;
   void* dk;
   void* dv;
-  int BH, N, D, nqt, nkv, has_cls;
+  int BH, H, N, D, nqt, nkv, has_cls;
   float c2, scale;
 };
 
@@ -241,13 +241,13 @@ __global__ void __launch_bounds__(kBsThreads, 1)
         const int nbh = bh + (int)gridDim.x;
         if (nbh < prm.BH) prefetch_l2_bytes(prm.lse + static_cast<size_t>(nbh) * N, N * 4);
         for (int i = 0; i < nqt; ++i) {
-          if (hl == 0) tma_prefetch_l2_3d(&tm_o, 0, i * kTile, bh);
+          if (hl == 0) tma_prefetch_l2_bh(&tm_o, 0, i * kTile, bh, prm.H);
           if (nbh < prm.BH) {
-            tma_prefetch_l2_3d(&tm_o, 0, i * kTile, nbh);
-            tma_prefetch_l2_3d(&tm_q, 0, i * kTile, nbh);
-            tma_prefetch_l2_3d(&tm_k, 0, i * kTile, nbh);
-            tma_prefetch_l2_3d(&tm_v, 0, i * kTile, nbh);
-            tma_prefetch_l2_3d(&tm_do, 0, i * kTile, nbh);
+            tma_prefetch_l2_bh(&tm_o, 0, i * kTile, nbh, prm.H);
+            tma_prefetch_l2_bh(&tm_q, 0, i * kTile, nbh, prm.H);
+            tma_prefetch_l2_bh(&tm_k, 0, i * kTile, nbh, prm.H);
+            tma_prefetch_l2_bh(&tm_v, 0, i * kTile, nbh, prm.H);
+            tma_prefetch_l2_bh(&tm_do, 0, i * kTile, nbh, prm.H);
           }
         }
         // Order Q0, K0, Q1, K1: the order in which the buffers are released.
@@ -255,12 +255,12 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           const int u = hl * nqt + t, sl = qslot(u);
           mbar_wait(&sm.q_empty[sl], qphase(u) ^ 1u, abort_flag);
           mbar_arrive_expect_tx(&sm.q_full[sl], 2 * kChunkBytes);
-          tma_load_3d(sm.q[sl], &tm_q, &sm.q_full[sl], 0, t * kTile, bh);
-          tma_load_3d(sm.dO[sl], &tm_do, &sm.q_full[sl], 0, t * kTile, bh);
+          tma_load_bh(sm.q[sl], &tm_q, &sm.q_full[sl], 0, t * kTile, bh, prm.H);
+          tma_load_bh(sm.dO[sl], &tm_do, &sm.q_full[sl], 0, t * kTile, bh, prm.H);
           mbar_wait(&sm.kv_empty[t], (hl & 1) ^ 1, abort_flag);
           mbar_arrive_expect_tx(&sm.kv_full[t], 2 * kChunkBytes);
-          tma_load_3d(sm.k[t], &tm_k, &sm.kv_full[t], 0, t * kTile, bh);
-          tma_load_3d(sm.v[t], &tm_v, &sm.kv_full[t], 0, t * kTile, bh);
+          tma_load_bh(sm.k[t], &tm_k, &sm.kv_full[t], 0, t * kTile, bh, prm.H);
+          tma_load_bh(sm.v[t], &tm_v, &sm.kv_full[t], 0, t * kTile, bh, prm.H);
         }
       }
     } else if (warp == 1 && lane == 0) {
@@ -463,7 +463,8 @@ __global__ void __launch_bounds__(kBsThreads, 1)
                 (isq && qv) ? prm.lse[static_cast<size_t>(tbh) * N + idx * kTile + r] : 0.f;
             mbar_wait(isq ? &sm.q_full[sl] : &sm.kv_full[idx], isq ? qphase(u) : (thl & 1),
                       abort_flag);
-            rotate_row_t<T>(smem_u32(isq ? sm.q[sl] : sm.k[idx]), smem_u32(sm.tab[idx]), r, D);
+            if (prm.has_cls >= 0)
+              rotate_row_t<T>(smem_u32(isq ? sm.q[sl] : sm.k[idx]), smem_u32(sm.tab[idx]), r, D);
             if (isq) {
               // Padded query rows get lse2 = +inf: their P and dS are exactly 0.
               const float l2 = qv ? lsev * 1.4426950408889634f : INFINITY;
@@ -484,7 +485,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
             named_bar(2, 128);
             if (leader) {
               mbar_arrive(&sm.dq_free[idx]);
-              tma_store_3d(&tm_dq, sm.q[sl], 0, idx * kTile, tbh);
+              tma_store_bh(&tm_dq, sm.q[sl], 0, idx * kTile, tbh, prm.H);
               tma_store_commit();
               tma_store_wait_read();
               mbar_arrive(&sm.q_empty[sl]);
@@ -504,8 +505,8 @@ __global__ void __launch_bounds__(kBsThreads, 1)
             named_bar(3, 128);
             if (leader) {
               mbar_arrive(&sm.acc_free);
-              tma_store_3d(&tm_dv, sm.v[idx], 0, idx * kTile, tbh);
-              tma_store_3d(&tm_dk, sm.k[idx], 0, idx * kTile, tbh);
+              tma_store_bh(&tm_dv, sm.v[idx], 0, idx * kTile, tbh, prm.H);
+              tma_store_bh(&tm_dk, sm.k[idx], 0, idx * kTile, tbh, prm.H);
               tma_store_commit();
               tma_store_wait_read();
               mbar_arrive(&sm.kv_empty[idx]);
@@ -557,6 +558,7 @@ cudaError_t launch_bwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
   p.dk = dk;
   p.dv = dv;
   p.BH = s.BH;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;

@@ -65,7 +65,7 @@ struct FwdParams {
   const float* sinp;
   void* o;
   float* lse;
-  int N, D, nqt, npair, nkv, has_cls;
+  int H, N, D, nqt, npair, nkv, has_cls;
   float c2;  // scale * log2(e)
 };
 
@@ -126,15 +126,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int g = 0; g < nact; ++g) {
         mbar_arrive_expect_tx(&sm.q_full[g], NCH * kChunkBytes);
         for (int c = 0; c < NCH; ++c)
-          tma_load_3d(sm.q[g][c], &tm_q, &sm.q_full[g], c * kChunkCols, (2 * pr + g) * kTile, bh);
+          tma_load_bh(sm.q[g][c], &tm_q, &sm.q_full[g], c * kChunkCols, (2 * pr + g) * kTile, bh, prm.H);
       }
       for (int j = 0; j < prm.nkv; ++j) {
         const int s = j % KS;
         mbar_wait(&sm.kv_empty[s], ((j / KS) & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.kv_full[s], 2 * NCH * kChunkBytes);
         for (int c = 0; c < NCH; ++c) {
-          tma_load_3d(sm.k[s][c], &tm_k, &sm.kv_full[s], c * kChunkCols, j * kTile, bh);
-          tma_load_3d(sm.v[s][c], &tm_v, &sm.kv_full[s], c * kChunkCols, j * kTile, bh);
+          tma_load_bh(sm.k[s][c], &tm_k, &sm.kv_full[s], c * kChunkCols, j * kTile, bh, prm.H);
+          tma_load_bh(sm.v[s][c], &tm_v, &sm.kv_full[s], c * kChunkCols, j * kTile, bh, prm.H);
         }
       }
     }
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         RopeQ<NCH, 16> rope;
         load_rope_q<NCH, 16>(rope, r0, tok0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
         if (blk == 0) mbar_wait(full, parity, abort_flag);
-        apply_rope_q<T, NCH, 16>(tile, r0, D, rope, lane);
+        if (prm.has_cls >= 0) apply_rope_q<T, NCH, 16>(tile, r0, D, rope, lane);
       }
     };
     for (int g = 0; g < nact; ++g)
@@ -413,6 +413,7 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.sinp = sinp;
   p.o = o;
   p.lse = lse;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;

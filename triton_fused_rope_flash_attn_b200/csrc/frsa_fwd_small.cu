@@ -57,7 +57,7 @@ struct FsParams {
   const float* sinp;
   void* o;
   float* lse;
-  int BH, N, D, nqt, nkv, has_cls;
+  int BH, H, N, D, nqt, nkv, has_cls;
   float c2;
 };
 
@@ -123,17 +123,17 @@ __global__ void __launch_bounds__(kFsThreads, 1)
         mbar_wait(&sm.q_empty[st], fp, abort_flag);
         mbar_arrive_expect_tx(&sm.q_full[st], nqt * kChunkBytes);
         for (int g = 0; g < nqt; ++g)
-          tma_load_3d(sm.q[st][g], &tm_q, &sm.q_full[st], 0, g * kTile, bh);
+          tma_load_bh(sm.q[st][g], &tm_q, &sm.q_full[st], 0, g * kTile, bh, prm.H);
         // Q and K are released when the score products of their head are
         // done, V after its last P V: loads run up to two heads ahead.
         mbar_wait(&sm.k_empty[st], fp, abort_flag);
         mbar_arrive_expect_tx(&sm.k_full[st], nkv * kChunkBytes);
         for (int j = 0; j < nkv; ++j)
-          tma_load_3d(sm.k[st][j], &tm_k, &sm.k_full[st], 0, j * kTile, bh);
+          tma_load_bh(sm.k[st][j], &tm_k, &sm.k_full[st], 0, j * kTile, bh, prm.H);
         mbar_wait(&sm.v_empty[st], fp, abort_flag);
         mbar_arrive_expect_tx(&sm.v_full[st], nkv * kChunkBytes);
         for (int j = 0; j < nkv; ++j)
-          tma_load_3d(sm.v[st][j], &tm_v, &sm.v_full[st], 0, j * kTile, bh);
+          tma_load_bh(sm.v[st][j], &tm_v, &sm.v_full[st], 0, j * kTile, bh, prm.H);
       }
     }
   } else if (warp == 1) {
@@ -226,14 +226,14 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       const uint32_t hp = (hl >> 1) & 1;
       // Rows past N were zero-filled by the loads and stay zero.
       mbar_wait(&sm.q_full[st], hp, abort_flag);
-      for (int rr = t; rr < N; rr += kFsRotThreads)
+      for (int rr = t; prm.has_cls >= 0 && rr < N; rr += kFsRotThreads)
         rotate_row_t<T, 4>(smem_u32(sm.q[st][rr >> 7]), smem_u32(sm.tab[rr >> 7]), rr & (kTile - 1),
                            D);
       fence_proxy_async_smem();
       named_bar(1, kFsRotThreads);
       if (t == 0) mbar_arrive(&sm.q_ready[st]);
       mbar_wait(&sm.k_full[st], hp, abort_flag);
-      for (int rr = t; rr < N; rr += kFsRotThreads)
+      for (int rr = t; prm.has_cls >= 0 && rr < N; rr += kFsRotThreads)
         rotate_row_t<T, 4>(smem_u32(sm.k[st][rr >> 7]), smem_u32(sm.tab[rr >> 7]), rr & (kTile - 1),
                            D);
       fence_proxy_async_smem();
@@ -399,6 +399,7 @@ cudaError_t launch_fwd_small_t(const LaunchShape& s, const CUtensorMap& tm_q,
   p.sinp = sinp;
   p.lse = lse;
   p.BH = s.BH;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;

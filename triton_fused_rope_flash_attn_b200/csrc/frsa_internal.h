@@ -14,9 +14,10 @@ constexpr int kChunkBytes = kTile * kChunkCols * 2;  // 16 KiB
 
 struct LaunchShape {
   int BH;        // B * H
+  int H;         // heads (maps address [B, H, N, D] tensors as {D, N, H, B})
   int N;         // sequence length
   int D;         // head dim (multiple of 8, <= 128)
-  int has_cls;
+  int has_cls;   // 0 or 1; -1: no RoPE (q and k arrive rotated, nothing is rotated)
   float scale;
   bool bf16;     // true: bf16, false: f16 (16-bit kernels)
   bool f32;      // float32 I/O and TF32 compute (the frsa_tf32.cu kernels)
@@ -74,9 +75,23 @@ int bwd_slots(const LaunchShape& s);
 // backward needs with `nslot` partial slots.
 size_t bwd_counter_ints(const LaunchShape& s, int nslot);
 
-// General backward: optional Delta pre-pass into delta_buf (then read by the
-// main kernel; when null the kernel forms Delta itself and writes `delta` if
-// given), then the persistent key-tile kernel with the ordered dQ reduction.
+// Rotation pre-pass of the general backward: q and k (element strides b, h,
+// n) are rotated once into contiguous buffers q_rot / k_rot, which the
+// kernel's maps tm_q / tm_k then cover.
+struct QkRotation {
+  const void* q;
+  const void* k;
+  long long q_strides[3];
+  long long k_strides[3];
+  void* q_rot;
+  void* k_rot;
+};
+
+// General backward: optional row pre-pass (rotation of q and k when `rot` is
+// given; Delta into delta_buf when that is non-null, then read by the main
+// kernel; when null the kernel forms Delta itself and writes `delta` if
+// given), then the persistent key-tile kernel with the ordered dQ reduction
+// (which rotates the Q and K tiles itself when `rot` is null).
 // dq_part: f32 [nslot, BH, N, D] partial sums (1 <= nslot <= key tiles);
 // counters: bwd_counter_ints(s, nslot) int32 words (cleared here on `stream`).
 // tm_dk / tm_dv: the usual maps over dK / dV; tm_part: f32 map {D, N, nslot*BH}
@@ -89,7 +104,7 @@ cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
                                const void* d_o, const float* lse, float* delta,
                                const float* cosp, const float* sinp, void* dq, void* dk, void* dv,
                                float* dq_part, int nslot, int* counters, float* delta_buf,
-                               cudaStream_t stream);
+                               const QkRotation* rot, cudaStream_t stream);
 
 // Number of SMs of the current device (queried once per device).
 int device_sm_count();

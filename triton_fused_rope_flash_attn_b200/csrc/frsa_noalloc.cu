@@ -108,7 +108,9 @@ extern "C" int frsa_bwd_noalloc(const frsa_attn_args* a, void* stream) {
   float* scratch = frsa::noalloc_scratch_ptr(&lookup);
   if (scratch == nullptr) return launch_error("frsa_bwd_noalloc: cudaGetSymbolAddress", lookup);
   CUtensorMap tq, tk, tv, tdo, to;
-  if (!encode_map(&tq, a->q, s) || !encode_map(&tk, a->k, s) || !encode_map(&tv, a->v, s) ||
+  if (!encode_map(&tq, a->q, s, false, strides_of(a->q_strides)) ||
+      !encode_map(&tk, a->k, s, false, strides_of(a->k_strides)) ||
+      !encode_map(&tv, a->v, s, false, strides_of(a->v_strides)) ||
       !encode_map(&tdo, a->d_o, s) || !encode_map(&to, a->o, s))
     return launch_error("frsa_bwd_noalloc", cudaSuccess);
   // Every shape (also N <= 256, D <= 64) runs the general key-tile kernel
@@ -121,6 +123,7 @@ extern "C" int frsa_bwd_noalloc(const frsa_attn_args* a, void* stream) {
     return launch_error("frsa_bwd_noalloc", cudaSuccess);
   const cudaError_t e = frsa::launch_bwd_ordered(
       s, tq, tk, tv, tdo, to, tdk, tdv, tpart, a->o, a->d_o, a->lse, a->delta, a->cosp, a->sinp,
-      a->dq, a->dk, a->dv, scratch, S, counters, a->delta, static_cast<cudaStream_t>(stream));
+      a->dq, a->dk, a->dv, scratch, S, counters, a->delta, /*rot=*/nullptr,
+      static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_bwd_noalloc", e);
 }

@@ -58,6 +58,10 @@ __device__ __forceinline__ uint64_t globaltimer() {
 #endif
 #ifdef FRSA_TRACE
 __device__ unsigned long long g_trace[2048 * 64];
+// Per-iteration stamps of kernels that record them: [cta][iteration] times
+// and event flags.
+__device__ unsigned long long g_trace_it[2048 * 1024];
+__device__ unsigned int g_trace_fl[2048 * 1024];
 #define FRSA_STAMP(slot)                                                       \
   do {                                                                         \
     if (blockIdx.x < 2048 && threadIdx.x == FRSA_STAMP_TID)                    \
@@ -237,6 +241,28 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// [B, H, N, D] tensors are addressed through 4-D maps {D, N, H, B} (any
+// b/h/n strides, unit d stride); a kernel names a head by its flat index
+// bh = b * H + h.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_bh(void* smem_dst, const void* tmap, uint64_t* bar, int x,
+                                            int y, int bh, int H) {
+  tma_load_4d(smem_dst, tmap, bar, x, y, bh % H, bh / H);
+}
+__device__ __forceinline__ void tma_prefetch_l2_bh(const void* tmap, int x, int y, int bh, int H) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(bh % H), "r"(bh / H)
+               : "memory");
+}
+
 // 2-D tiled load global -> shared, completing on `bar` (transaction bytes).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x,
                                             int y) {
@@ -281,6 +307,14 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
       "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::
           "l"(reinterpret_cast<uint64_t>(tmap)),
       "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_bh(const void* tmap, const void* smem_src, int x, int y,
+                                             int bh, int H) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(bh % H), "r"(bh / H)
       : "memory");
 }
 __device__ __forceinline__ void tma_store_commit() {

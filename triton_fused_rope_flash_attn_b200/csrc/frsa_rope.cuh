@@ -25,8 +25,9 @@
 namespace frsa {
 
 // Table row index of token `t`, or -1 when the token is not rotated.
+// has_cls < 0 marks a call without RoPE (q and k arrive rotated): no token is.
 __device__ __forceinline__ int rope_pos(int t, int N, int has_cls) {
-  if (t >= N) return -1;
+  if (t >= N || has_cls < 0) return -1;
   if (has_cls && t == 0) return -1;
   return t - has_cls;
 }

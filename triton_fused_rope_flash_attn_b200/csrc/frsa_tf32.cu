@@ -127,7 +127,7 @@ struct T32FwdParams {
   const float* sinp;
   float* o;
   float* lse;
-  int N, D, nqt, nkv, has_cls;
+  int H, N, D, nqt, nkv, has_cls;
   float c2;
 };
 
@@ -189,14 +189,14 @@ __global__ void __launch_bounds__(kT32Threads, 1)
       tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(&sm.q_full, NC * kChunkBytes);
       for (int c = 0; c < NC; ++c)
-        tma_load_3d(sm.q[c], &tm_q, &sm.q_full, 32 * c, qt * kTile, bh);
+        tma_load_bh(sm.q[c], &tm_q, &sm.q_full, 32 * c, qt * kTile, bh, prm.H);
       for (int j = 0; j < nkv; ++j) {
         const int s = j % KS;
         mbar_wait(&sm.kv_empty[s], ((j / KS) & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.kv_full[s], 2 * NC * kChunkBytes);
         for (int c = 0; c < NC; ++c) {
-          tma_load_3d(sm.k[s][c], &tm_k, &sm.kv_full[s], 32 * c, j * kTile, bh);
-          tma_load_3d(sm.v[s][c], &tm_v, &sm.kv_full[s], 32 * c, j * kTile, bh);
+          tma_load_bh(sm.k[s][c], &tm_k, &sm.kv_full[s], 32 * c, j * kTile, bh, prm.H);
+          tma_load_bh(sm.v[s][c], &tm_v, &sm.kv_full[s], 32 * c, j * kTile, bh, prm.H);
         }
       }
     }
@@ -349,6 +349,7 @@ cudaError_t launch_fwd_tf32_t(const LaunchShape& s, const CUtensorMap& tm_q,
   p.sinp = sinp;
   p.o = o;
   p.lse = lse;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;
@@ -459,7 +460,7 @@ struct T32BwdParams {
   float* dq;
   float* dk;
   float* dv;
-  int N, D, nqt, nkv, has_cls;
+  int H, N, D, nqt, nkv, has_cls;
   float c2, scale;
 };
 
@@ -528,17 +529,17 @@ __global__ void __launch_bounds__(kT32Threads, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(&sm.kv_full, 2 * NC * kChunkBytes);
       for (int c = 0; c < NC; ++c) {
-        tma_load_3d(sm.k[c], &tm_k16, &sm.kv_full, 32 * c, jt * kTile, bh);
-        tma_load_3d(sm.v[c], &tm_v16, &sm.kv_full, 32 * c, jt * kTile, bh);
+        tma_load_bh(sm.k[c], &tm_k16, &sm.kv_full, 32 * c, jt * kTile, bh, prm.H);
+        tma_load_bh(sm.v[c], &tm_v16, &sm.kv_full, 32 * c, jt * kTile, bh, prm.H);
       }
       for (int i = 0; i < nqt; ++i) {
         mbar_wait(&sm.q_empty, (i & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.q_full, 4 * NC * kChunkBytes);
         for (int c = 0; c < NC; ++c) {
-          tma_load_3d(sm.qa[c], &tm_q16, &sm.q_full, 32 * c, i * kTile, bh);
-          tma_load_3d(sm.qb[c], &tm_q32, &sm.q_full, 32 * c, i * kTile, bh);
-          tma_load_3d(sm.da[c], &tm_do16, &sm.q_full, 32 * c, i * kTile, bh);
-          tma_load_3d(sm.db[c], &tm_do32, &sm.q_full, 32 * c, i * kTile, bh);
+          tma_load_bh(sm.qa[c], &tm_q16, &sm.q_full, 32 * c, i * kTile, bh, prm.H);
+          tma_load_bh(sm.qb[c], &tm_q32, &sm.q_full, 32 * c, i * kTile, bh, prm.H);
+          tma_load_bh(sm.da[c], &tm_do16, &sm.q_full, 32 * c, i * kTile, bh, prm.H);
+          tma_load_bh(sm.db[c], &tm_do32, &sm.q_full, 32 * c, i * kTile, bh, prm.H);
         }
       }
     }
@@ -711,16 +712,16 @@ __global__ void __launch_bounds__(kT32Threads, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(&sm.q_full, 2 * NC * kChunkBytes);
       for (int c = 0; c < NC; ++c) {
-        tma_load_3d(sm.q[c], &tm_q16, &sm.q_full, 32 * c, it * kTile, bh);
-        tma_load_3d(sm.d[c], &tm_do16, &sm.q_full, 32 * c, it * kTile, bh);
+        tma_load_bh(sm.q[c], &tm_q16, &sm.q_full, 32 * c, it * kTile, bh, prm.H);
+        tma_load_bh(sm.d[c], &tm_do16, &sm.q_full, 32 * c, it * kTile, bh, prm.H);
       }
       for (int j = 0; j < nkv; ++j) {
         mbar_wait(&sm.kv_empty, (j & 1) ^ 1, abort_flag);
         mbar_arrive_expect_tx(&sm.kv_full, 3 * NC * kChunkBytes);
         for (int c = 0; c < NC; ++c) {
-          tma_load_3d(sm.ka[c], &tm_k16, &sm.kv_full, 32 * c, j * kTile, bh);
-          tma_load_3d(sm.kb[c], &tm_k32, &sm.kv_full, 32 * c, j * kTile, bh);
-          tma_load_3d(sm.v[c], &tm_v16, &sm.kv_full, 32 * c, j * kTile, bh);
+          tma_load_bh(sm.ka[c], &tm_k16, &sm.kv_full, 32 * c, j * kTile, bh, prm.H);
+          tma_load_bh(sm.kb[c], &tm_k32, &sm.kv_full, 32 * c, j * kTile, bh, prm.H);
+          tma_load_bh(sm.v[c], &tm_v16, &sm.kv_full, 32 * c, j * kTile, bh, prm.H);
         }
       }
     }
@@ -842,6 +843,7 @@ cudaError_t launch_bwd_tf32_t(const LaunchShape& s, const CUtensorMap* maps, con
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
+  p.H = s.H;
   p.N = s.N;
   p.D = s.D;
   p.nqt = (s.N + kTile - 1) / kTile;

@@ -5,10 +5,10 @@ attention block does before the attention (reference README:156-159: timm's
 ``qkv = Linear(x)``, head split, RoPE on q and k) in one sm_100a kernel
 (``frsa_qkv_rope`` of the C ABI): a tcgen05 GEMM whose epilogue adds the bias,
 rotates q and k by token position and writes q, k, v as ``[B, H, N, D]``.
-The attention over these q, k then uses identity tables (``IDENTITY``-style
-tables from ``identity_tables``), so the rotation leaves the attention
-kernels. The backward applies ``R^T`` to dq and dk and uses torch GEMMs for
-dx, dW and db.
+The attention over these q, k then runs with ``rope=False`` (the C ABI's
+FRSA_FLAG_NO_ROPE: the kernels rotate nothing), so the rotation leaves the
+attention kernels. The backward applies ``R^T`` to dq and dk and uses torch
+GEMMs for dx, dW and db.
 """
 from __future__ import annotations
 
@@ -88,15 +88,3 @@ def qkv_rope(x, weight, bias, cos_sin, num_heads: int, has_cls: bool = True):
     COSP, SINP = cos_sin.tables()
     return QKVRope.apply(x, weight, bias, COSP.contiguous(), SINP.contiguous(), num_heads,
                          has_cls)
-
-
-class IdentityTables(torch.nn.Module):
-    """Tables with cos = 1, sin = 0: attention over already-rotated q and k."""
-
-    def __init__(self, n_pos: int, D: int, device):
-        super().__init__()
-        self.register_buffer("COSP", torch.ones(n_pos, D // 2, device=device))
-        self.register_buffer("SINP", torch.zeros(n_pos, D // 2, device=device))
-
-    def tables(self):
-        return self.COSP, self.SINP
