@@ -167,3 +167,28 @@ def test_torch_extension_builds_binds_and_rejects_cpu_tensors():
     tab = torch.zeros(4, 32)
     with pytest.raises(RuntimeError, match="CUDA"):
         fused_rope_attention_fwd(q, q, q, tab, tab, True)
+
+
+def test_strides_and_flags_validated(lib):
+    """q/k/v strides (b, h, n in elements) must be positive multiples of 16
+    bytes; unknown flag bits are refused; FRSA_FLAG_NO_ROPE needs no tables."""
+    def code(a):
+        return lib.frsa_fwd(ctypes.byref(a), None)
+
+    ok = _args(H=2)
+    ok.q_strides[:] = [197 * 3 * 2 * 64, 64, 3 * 2 * 64]   # a [B, N, 3, H, D] view
+    assert code(ok) == 8                                    # valid: no sm_100 device here
+    bad = _args(H=2)
+    bad.q_strides[:] = [197 * 3 * 2 * 64, 60, 3 * 2 * 64]  # 120-byte head stride
+    assert code(bad) == 5
+    neg = _args()
+    neg.k_strides[:] = [0, 0, -64]
+    assert code(neg) == 5
+    flags = _args(flags=2)
+    assert code(flags) == 2
+    norope = _args(flags=_lib.FRSA_FLAG_NO_ROPE, n_pos=0)
+    norope.cosp = norope.sinp = None
+    assert code(norope) == 8                                # tables not needed
+    rope = _args(n_pos=0)
+    rope.cosp = rope.sinp = None
+    assert code(rope) == 1                                  # tables needed

@@ -92,8 +92,8 @@ struct BwdSmem {
   // tiles, then the f32 dQ^ share); with one query stage the P/dS tiles,
   // which are idle while results drain, serve instead.
   uint8_t stage[(NCH == 1) ? 2 : 1][kChunkBytes];
-  float lse2[QS][kTile];       // lse * log2(e) of the query tile
-  float delta[QS][kTile];
+  alignas(16) float lse2[QS][kTile];   // lse * log2(e) of the query tile (read as float4)
+  alignas(16) float delta[QS][kTile];
   uint64_t kv_full[KVS], kv_empty[KVS];
   uint64_t q_full[QS], q_empty[QS];
   uint64_t kq_ready, st_full, st_free, ds_full, mm_done, dq_free, acc_free;
@@ -147,39 +147,33 @@ __device__ __forceinline__ void complete_dq_tile(const BwdParams& prm, int bh, i
   const int q0 = i * kTile;
   T* dq_head = reinterpret_cast<T*>(prm.dq) + static_cast<size_t>(bh) * head_elems;
   const float* part0 = prm.dq_part + static_cast<size_t>(bh) * head_elems;
-  // QB of the warp's quads of rows are summed together, one slot per round
-  // (2 QB loads in flight per lane): a completion costs S L2 round trips per
-  // group of quads and 64-column chunk.
-  constexpr int KQ = RW / 4;               // quads per warp
-  constexpr int QB = (NCH == 1) ? KQ : 2;  // quads per round
-#pragma unroll 1
-  for (int hk = 0; hk < NCH * (KQ / QB); ++hk) {
-    const int h = hk / (KQ / QB), k0 = (hk - h * (KQ / QB)) * QB;
-    const int gg = gl + 8 * h;
-    if (8 * gg >= D) continue;
-    float v[QB][8];
-    const float4* src[QB];
-    bool ok[QB];
+  constexpr int KQ = RW / 4;   // quads of rows per warp
+  if constexpr (NCH == 1) {
+    // The warp's four quads are summed together, one slot per round (8
+    // loads in flight per lane): S L2 round trips per completion.
+    float v[KQ][8];
+    const float4* src[KQ];
+    bool ok[KQ];
 #pragma unroll
-    for (int k = 0; k < QB; ++k) {
-      const int tk = q0 + rw0 + 4 * (k0 + k) + rq;
-      ok[k] = tk < N;
+    for (int k = 0; k < KQ; ++k) {
+      const int tk = q0 + rw0 + 4 * k + rq;
+      ok[k] = tk < N && 8 * gl < D;
       src[k] = reinterpret_cast<const float4*>(part0 + static_cast<size_t>(ok[k] ? tk : 0) * D +
-                                               8 * gg);
+                                               8 * gl);
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
     }
 #pragma unroll 1
     for (int sl = 0; sl < S; ++sl) {
-      float4 a[QB], bq[QB];
+      float4 a[KQ], bq[KQ];
 #pragma unroll
-      for (int k = 0; k < QB; ++k)
+      for (int k = 0; k < KQ; ++k)
         if (ok[k]) {
           a[k] = __ldcg(src[k] + sl * (slot_stride / 4));
           bq[k] = __ldcg(src[k] + sl * (slot_stride / 4) + 1);
         }
 #pragma unroll
-      for (int k = 0; k < QB; ++k)
+      for (int k = 0; k < KQ; ++k)
         if (ok[k]) {
           // slot order: v starts at 0, and 0 + x == x
           v[k][0] += a[k].x; v[k][1] += a[k].y; v[k][2] += a[k].z; v[k][3] += a[k].w;
@@ -187,16 +181,53 @@ __device__ __forceinline__ void complete_dq_tile(const BwdParams& prm, int bh, i
         }
     }
 #pragma unroll
-    for (int k = 0; k < QB; ++k) {
-      const int tk = q0 + rw0 + 4 * (k0 + k) + rq;
+    for (int k = 0; k < KQ; ++k) {
+      const int tk = q0 + rw0 + 4 * k + rq;
       if (!ok[k]) continue;
       const int p2 = rope_pos(tk, N, prm.has_cls);
       if (p2 >= 0) {
         const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
-        unrotate8(v[k], __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
+        unrotate8(v[k], __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gl),
+                  __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gl));
+      }
+      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gl) = pack8<T>(v[k]);
+    }
+  } else {
+    // One granule at a time, four slots' loads in flight: KQ * NCH *
+    // ceil(S / 4) L2 round trips per completion.
+#pragma unroll 1
+    for (int kh = 0; kh < KQ * NCH; ++kh) {
+      const int k = kh / NCH, h = kh - k * NCH;
+      const int tk = q0 + rw0 + 4 * k + rq;
+      const int gg = gl + 8 * h;
+      if (tk >= N || 8 * gg >= D) continue;
+      const float4* src =
+          reinterpret_cast<const float4*>(part0 + static_cast<size_t>(tk) * D + 8 * gg);
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s0 = 0; s0 < kMaxDqSlots; s0 += 4) {
+        if (s0 >= S) break;
+        float4 a[4], bq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (s0 + u < S) {
+            a[u] = __ldcg(src + (s0 + u) * (slot_stride / 4));
+            bq[u] = __ldcg(src + (s0 + u) * (slot_stride / 4) + 1);
+          }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (s0 + u < S) {
+            v[0] += a[u].x; v[1] += a[u].y; v[2] += a[u].z; v[3] += a[u].w;
+            v[4] += bq[u].x; v[5] += bq[u].y; v[6] += bq[u].z; v[7] += bq[u].w;
+          }
+      }
+      const int p2 = rope_pos(tk, N, prm.has_cls);
+      if (p2 >= 0) {
+        const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
+        unrotate8(v, __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
                   __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gg));
       }
-      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) = pack8<T>(v[k]);
+      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) = pack8<T>(v);
     }
   }
   named_bar(1, kComputeThreads);

@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // P buffer b was last read by the P V of tile j - PB.
         if (j >= PB) mbar_wait(&sm.o_full[g][b], ((j - PB) / PB) & 1, abort_flag);
         tc_fence_after();
-        if (j == 0) FRSA_STAMP(4);
+        if (j < 12) FRSA_STAMP(8 + 2 * j);
         if (warp_active) {
           // pass 1: row max over the valid columns
           float mx = -INFINITY;
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_before();
         named_bar(2 + g, 128);
         if (leader) mbar_arrive(&sm.p_full[g]);
-        if (j == 0) FRSA_STAMP(5);
+        if (j < 12) FRSA_STAMP(9 + 2 * j);
       }
       FRSA_STAMP(7);
 
