@@ -1,15 +1,20 @@
 // Forward kernel: O = softmax(R(Q) R(K)^T * scale) V with 2D RoPE fused.
 //
 // Restates the computation of _attn_fwd (fa_rope_full .py:91-315) as a
-// warp-specialised tcgen05 kernel. One CTA owns a pair of 128-query tiles of
-// one (batch*head) (the whole head when N <= 256) and walks the keys in
-// 128-key tiles with an online softmax in base 2. The two query tiles share
-// every K/V load and K rotation.
+// persistent, warp-specialised tcgen05 kernel. A unit is a pair of 128-query
+// tiles of one (batch*head) (the whole head when N <= 256); each CTA walks
+// its units (see fwd_grid for the order) and, per unit, the keys in 128-key
+// tiles with an online softmax in base 2. The two query tiles share every
+// K/V load and K rotation, and the K/V stream runs on across units: the next
+// unit's query tiles load and rotate while this unit's last tile is in its
+// softmax and epilogue.
 //
-//   warp 0      TMA producer: the two Q tiles once, then K/V tiles into a
-//               ring of KS stages
+//   warp 0      TMA producer: each unit's query tiles, then K and V tiles into
+//               rings of KS stages (K and V released separately: K once the
+//               score products have read it, V once the P V products have)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..3, 12..13  rotation warps: apply RoPE in shared memory to the Q
+//   warps 2..3  no role (they complete warpgroup 0 for the register split)
+//   warps 12..15  rotation warps: apply RoPE in shared memory to the Q
 //               tiles and to every K tile as soon as TMA has landed it
 //   warps 4..11 two compute warpgroups, warpgroup g owns query tile g of the
 //               pair: it reads S from TMEM (thread = query row), writes P
@@ -36,23 +41,25 @@ namespace frsa {
 namespace {
 
 constexpr int kFwdCompute = 256;                // two warpgroups
-constexpr int kFwdThreads = 128 + kFwdCompute + 64;  // + producer, MMA, four rotation warps
+constexpr int kFwdThreads = 128 + kFwdCompute + 128;  // + producer/MMA warpgroup, rotation warpgroup
+// Registers per thread after the per-warpgroup split (launch: 128 each, 512
+// threads; 96 + 96 + 2 x 160 = 4 x 128).
+constexpr uint32_t kFwdRegsCtl = 96, kFwdRegsRot = 96, kFwdRegsCompute = 160;
 constexpr uint32_t kTmemColsFwd = 512;
-constexpr float kFwdSlack = 8.f;   // log2 headroom of the softmax base
+constexpr float kFwdSlack = 8.f;
+constexpr int kFwdMaxWaves = 12;   // chunk-size levels of the guided schedule   // log2 headroom of the softmax base
 
 template <int NCH>
 struct FwdSmem {
-  static constexpr int KS = (NCH == 1) ? 2 : 1;  // K/V ring stages
+  static constexpr int KS = (NCH == 1) ? 2 : 1;  // K and V ring stages
   static constexpr int PB = (NCH == 1) ? 2 : 1;  // P buffers per warpgroup
   uint8_t q[2][NCH][kChunkBytes];      // query tile of warpgroup g
   uint8_t k[KS][NCH][kChunkBytes];     // key ring
   uint8_t v[KS][NCH][kChunkBytes];     // value ring
   uint8_t p[2][PB][2][kChunkBytes];    // P tiles of warpgroup g: [128 q][128 kv], two chunks
-  uint64_t q_full[2];
-  uint64_t q_ready;
-  uint64_t kv_full[KS];
-  uint64_t kv_empty[KS];
-  uint64_t k_ready[KS];
+  uint64_t q_full[2], q_ready[2], q_empty[2];
+  uint64_t k_full[KS], k_ready[KS], k_empty[KS];
+  uint64_t v_full[KS], v_empty[KS];
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_full[2][PB];              // P V of a tile using P buffer b has completed
@@ -66,8 +73,36 @@ struct FwdParams {
   void* o;
   float* lse;
   int H, N, D, nqt, npair, nkv, has_cls;
-  float c2;  // scale * log2(e)
+  int nunits;  // BH * npair
+  float c2;    // scale * log2(e)
+  // Guided schedule (fwd_schedule): wave w holds CTAs [wcta[w], wcta[w+1])
+  // and gives each a run of wchunk[w] consecutive units starting at wunit[w].
+  int nwaves;
+  int wcta[kFwdMaxWaves + 1];
+  int wunit[kFwdMaxWaves];
+  int wchunk[kFwdMaxWaves];
 };
+
+// Units [begin, end) of this CTA.
+__device__ __forceinline__ void fwd_range(const FwdParams& prm, int& begin, int& end) {
+  const int b = static_cast<int>(blockIdx.x);
+  int w = 0;
+  while (w + 1 < prm.nwaves && b >= prm.wcta[w + 1]) ++w;
+  begin = prm.wunit[w] + (b - prm.wcta[w]) * prm.wchunk[w];
+  end = min(begin + prm.wchunk[w], prm.nunits);
+}
+
+// Unit u -> (head bh, pair pr, active query tiles of the pair: 1 or 2).
+struct FwdUnit {
+  int bh, pr, nact;
+};
+__device__ __forceinline__ FwdUnit fwd_unit(const FwdParams& prm, int u) {
+  FwdUnit x;
+  x.bh = u / prm.npair;
+  x.pr = u - x.bh * prm.npair;
+  x.nact = min(2, prm.nqt - 2 * x.pr);
+  return x;
+}
 
 template <typename T, int NCH>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -83,27 +118,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x / prm.npair;
-  const int pr = blockIdx.x - bh * prm.npair;
   const int N = prm.N, D = prm.D;
+  const int nkv = prm.nkv;
   const int DP = (D + 15) & ~15;   // MMA N for P V
   const int ksteps = DP >> 4;      // MMA K steps over the head dim
-  const int nact = min(2, prm.nqt - 2 * pr);  // active query tiles in this pair (1 or 2)
   volatile int* abort_flag = &sm.abort_flag;
+  int ubeg, uend;
+  fwd_range(prm, ubeg, uend);
 
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_ready[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
       mbar_init(&sm.p_full[s], 1);
       for (int b = 0; b < Sm::PB; ++b) mbar_init(&sm.o_full[s][b], 1);
     }
-    mbar_init(&sm.q_ready, 1);
     for (int s = 0; s < KS; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_ready[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
     }
     fence_mbar_init();
   }
@@ -117,36 +155,53 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  // Barrier phases. Query-tile buffer g is filled once per unit in which
+  // query tile g of the pair exists (fill f: parity f & 1); the K/V tiles
+  // form one running sequence t over the CTA's units (stage t % KS, parity
+  // (t / KS) & 1); warpgroup g's S / P / O barriers count the key tiles it
+  // has processed.
+  if (warp < 4) {
+  setmaxnreg_dec<kFwdRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      for (int g = 0; g < nact; ++g) {
-        mbar_arrive_expect_tx(&sm.q_full[g], NCH * kChunkBytes);
-        for (int c = 0; c < NCH; ++c)
-          tma_load_bh(sm.q[g][c], &tm_q, &sm.q_full[g], c * kChunkCols, (2 * pr + g) * kTile, bh, prm.H);
-      }
-      for (int j = 0; j < prm.nkv; ++j) {
-        const int s = j % KS;
-        mbar_wait(&sm.kv_empty[s], ((j / KS) & 1) ^ 1, abort_flag);
-        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * NCH * kChunkBytes);
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_bh(sm.k[s][c], &tm_k, &sm.kv_full[s], c * kChunkCols, j * kTile, bh, prm.H);
-          tma_load_bh(sm.v[s][c], &tm_v, &sm.kv_full[s], c * kChunkCols, j * kTile, bh, prm.H);
+      int qf[2] = {0, 0};
+      int t = 0;
+      for (int u = ubeg; u < uend; ++u) {
+        const FwdUnit x = fwd_unit(prm, u);
+        for (int g = 0; g < x.nact; ++g) {
+          mbar_wait(&sm.q_empty[g], (qf[g] & 1) ^ 1, abort_flag);
+          mbar_arrive_expect_tx(&sm.q_full[g], NCH * kChunkBytes);
+          for (int c = 0; c < NCH; ++c)
+            tma_load_bh(sm.q[g][c], &tm_q, &sm.q_full[g], c * kChunkCols, (2 * x.pr + g) * kTile,
+                        x.bh, prm.H);
+          ++qf[g];
+        }
+        for (int j = 0; j < nkv; ++j, ++t) {
+          const int s = t % KS;
+          const uint32_t ph = ((t / KS) & 1) ^ 1;
+          mbar_wait(&sm.k_empty[s], ph, abort_flag);
+          mbar_arrive_expect_tx(&sm.k_full[s], NCH * kChunkBytes);
+          for (int c = 0; c < NCH; ++c)
+            tma_load_bh(sm.k[s][c], &tm_k, &sm.k_full[s], c * kChunkCols, j * kTile, x.bh, prm.H);
+          mbar_wait(&sm.v_empty[s], ph, abort_flag);
+          mbar_arrive_expect_tx(&sm.v_full[s], NCH * kChunkBytes);
+          for (int c = 0; c < NCH; ++c)
+            tma_load_bh(sm.v[s][c], &tm_v, &sm.v_full[s], c * kChunkCols, j * kTile, x.bh, prm.H);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && ubeg < uend) {
       constexpr bool kBf = Elt<T>::kBf16;
       const uint32_t idS = idesc_f16(kBf, 128, 128, false, false);
       const uint32_t idO = idesc_f16(kBf, 128, DP, false, true);
       // S_g = Q^_g K^T : A = Q^ [q][d] K-major, B = K^ [kv][d] K-major.
-      auto issue_s = [&](int g, int j) {
-        const int s = j % KS;
+      auto issue_s = [&](int g, int s) {
         const uint32_t tS = tmem + 256 * g;
         for (int ks = 0; ks < ksteps; ++ks) {
           const int c = ks >> 2;
@@ -156,85 +211,143 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(&sm.s_full[g]);
       };
-      // O_g += P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major. O
-      // accumulates over the key tiles in TMEM.
-      auto issue_pv = [&](int g, int j) {
-        const int s = j % KS, b = j % PB;
+      // O_g (+)= P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major. O
+      // accumulates over the key tiles of a unit in TMEM.
+      auto issue_pv = [&](int g, int s, int b, bool acc) {
         const uint32_t tO = tmem + 256 * g + 128;
         for (int ks = 0; ks < kTile / 16; ++ks) {
           mma_ss(tO, sw128_desc(smem_u32(sm.p[g][b][ks >> 2]) + (ks & 3) * 32, 16, 1024),
                  sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024), idO,
-                 (j | ks) > 0);
+                 acc || ks > 0);
         }
         mma_commit(&sm.o_full[g][b]);
       };
-      mbar_wait(&sm.q_ready, 0, abort_flag);
+      int qf[2] = {0, 0};   // query-tile fill of the current unit, per warpgroup
+      int tg[2] = {0, 0};   // key tiles processed, per warpgroup
+      int t = 0;            // running K/V tile
+      int u = ubeg;
+      FwdUnit x = fwd_unit(prm, u);
+      // Prologue: the first unit's scores against its first key tile.
       mbar_wait(&sm.k_ready[0], 0, abort_flag);
-      tc_fence_after();
-      for (int g = 0; g < nact; ++g) issue_s(g, 0);
-      for (int j = 0; j < prm.nkv; ++j) {
-        const bool more = j + 1 < prm.nkv;
-        if (KS == 1) {
-          // One K/V stage: tile j+1 can only land after every P V of tile j.
-          for (int g = 0; g < nact; ++g) {
-            mbar_wait(&sm.p_full[g], j & 1, abort_flag);
-            tc_fence_after();
-            issue_pv(g, j);
-          }
-          mma_commit(&sm.kv_empty[0]);
-          if (more) {
-            mbar_wait(&sm.k_ready[0], (j + 1) & 1, abort_flag);
-            tc_fence_after();
-            for (int g = 0; g < nact; ++g) issue_s(g, j + 1);
-          }
-        } else {
-          // S_g of tile j+1 goes ahead of P_g V of tile j (P is in shared
-          // memory, so S may overwrite the scores as soon as the softmax has
-          // published P): the group's next softmax overlaps this P V.
-          for (int g = 0; g < nact; ++g) {
-            mbar_wait(&sm.p_full[g], j & 1, abort_flag);
-            tc_fence_after();
-            if (more) {
-              if (g == 0) {
-                mbar_wait(&sm.k_ready[(j + 1) % KS], ((j + 1) / KS) & 1, abort_flag);
-                tc_fence_after();
-              }
-              issue_s(g, j + 1);
+      for (int g = 0; g < x.nact; ++g) {
+        mbar_wait(&sm.q_ready[g], 0, abort_flag);
+        tc_fence_after();
+        issue_s(g, 0);
+        if (nkv == 1) mma_commit(&sm.q_empty[g]);
+      }
+      mma_commit(&sm.k_empty[0]);
+      for (;;) {
+        const int un = u + 1;
+        const bool has_next = un < uend;
+        const FwdUnit xn = fwd_unit(prm, has_next ? un : u);
+        for (int j = 0; j < nkv; ++j, ++t) {
+          const int s = t % KS;
+          const bool more = j + 1 < nkv;
+          const int t1 = t + 1, s1 = t1 % KS;
+          bool k_waited = false, v_waited = false;
+          bool any_s = false;
+          auto wait_v = [&]() {
+            if (!v_waited) {
+              mbar_wait(&sm.v_full[s], (t / KS) & 1, abort_flag);
+              tc_fence_after();
+              v_waited = true;
             }
-            issue_pv(g, j);
+          };
+          auto wait_k = [&]() {
+            if (!k_waited) {
+              mbar_wait(&sm.k_ready[s1], (t1 / KS) & 1, abort_flag);
+              k_waited = true;
+            }
+          };
+          if (more) {
+            // S_g of the next key tile goes ahead of P_g V of this tile: P is
+            // in shared memory, so S may overwrite the scores as soon as the
+            // softmax has published P, and the group's next softmax overlaps
+            // this P V.
+            for (int g = 0; g < x.nact; ++g) {
+              mbar_wait(&sm.p_full[g], tg[g] & 1, abort_flag);
+              tc_fence_after();
+              wait_k();
+              tc_fence_after();
+              issue_s(g, s1);
+              // The last score product of a query tile frees its buffer.
+              if (j + 2 == nkv) mma_commit(&sm.q_empty[g]);
+              any_s = true;
+              wait_v();
+              issue_pv(g, s, tg[g] % PB, j > 0);
+              ++tg[g];
+            }
+          } else {
+            // Last key tile of the unit: its P V products go first, so that
+            // the epilogue never waits for the next unit's query tiles to
+            // land and rotate; then the next unit's first scores.
+            for (int g = 0; g < x.nact; ++g) {
+              mbar_wait(&sm.p_full[g], tg[g] & 1, abort_flag);
+              tc_fence_after();
+              wait_v();
+              issue_pv(g, s, tg[g] % PB, j > 0);
+              ++tg[g];
+            }
+            if (has_next) {
+              for (int g = 0; g < xn.nact; ++g) {
+                wait_k();
+                mbar_wait(&sm.q_ready[g], (qf[g] + (g < x.nact ? 1 : 0)) & 1, abort_flag);
+                tc_fence_after();
+                issue_s(g, s1);
+                if (nkv == 1) mma_commit(&sm.q_empty[g]);
+                any_s = true;
+              }
+            }
           }
-          mma_commit(&sm.kv_empty[j % KS]);
+          if (any_s) mma_commit(&sm.k_empty[s1]);
+          mma_commit(&sm.v_empty[s]);
         }
+        for (int g = 0; g < x.nact; ++g) ++qf[g];
+        if (!has_next) break;
+        u = un;
+        x = xn;
       }
     }
-  } else if (warp < 4 || warp >= 12) {
+  }   // warps 2 and 3 have no role
+  } else if (warp >= 12) {
+    setmaxnreg_dec<kFwdRegsRot>();
     // ------------------------------------------------------------ rotation warps
-    // Warps 2, 3, 12, 13; each rotates a quarter of every tile, 16 rows at a
-    // time with the table values loaded before the tile's TMA wait.
-    const int rwp = warp < 4 ? warp - 2 : warp - 10;
+    // Warps 12..15; each rotates a quarter of every tile, 16 rows (8
+    // when D > 64) at a time with the table values loaded before the tile's
+    // TMA wait.
+    constexpr int kRows = 16 / NCH;
+    const int rwp = warp - 12;
     auto rotate_tile = [&](uint8_t* tile, int tok0, uint64_t* full, uint32_t parity) {
 #pragma unroll 1
-      for (int blk = 0; blk < 2; ++blk) {
-        const int r0 = rwp * 32 + blk * 16;
-        RopeQ<NCH, 16> rope;
-        load_rope_q<NCH, 16>(rope, r0, tok0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
+      for (int blk = 0; blk < 32 / kRows; ++blk) {
+        const int r0 = rwp * 32 + blk * kRows;
+        RopeQ<NCH, kRows> rope;
+        load_rope_q<NCH, kRows>(rope, r0, tok0, N, prm.has_cls, D, prm.cosp, prm.sinp, lane);
         if (blk == 0) mbar_wait(full, parity, abort_flag);
-        if (prm.has_cls >= 0) apply_rope_q<T, NCH, 16>(tile, r0, D, rope, lane);
+        if (prm.has_cls >= 0) apply_rope_q<T, NCH, kRows>(tile, r0, D, rope, lane);
       }
     };
-    for (int g = 0; g < nact; ++g)
-      rotate_tile(&sm.q[g][0][0], (2 * pr + g) * kTile, &sm.q_full[g], 0);
-    fence_proxy_async_smem();
-    named_bar(1, 128);
-    if (threadIdx.x == 64) mbar_arrive(&sm.q_ready);
-    for (int j = 0; j < prm.nkv; ++j) {
-      const int s = j % KS;
-      rotate_tile(&sm.k[s][0][0], j * kTile, &sm.kv_full[s], (j / KS) & 1);
-      fence_proxy_async_smem();
-      named_bar(1, 128);
-      if (threadIdx.x == 64) mbar_arrive(&sm.k_ready[s]);
+    int qf[2] = {0, 0};
+    int t = 0;
+    for (int u = ubeg; u < uend; ++u) {
+      const FwdUnit x = fwd_unit(prm, u);
+      for (int g = 0; g < x.nact; ++g) {
+        rotate_tile(&sm.q[g][0][0], (2 * x.pr + g) * kTile, &sm.q_full[g], qf[g] & 1);
+        ++qf[g];
+        fence_proxy_async_smem();
+        named_bar(1, 128);
+        if (threadIdx.x == 384) mbar_arrive(&sm.q_ready[g]);
+      }
+      for (int j = 0; j < nkv; ++j, ++t) {
+        const int s = t % KS;
+        rotate_tile(&sm.k[s][0][0], j * kTile, &sm.k_full[s], (t / KS) & 1);
+        fence_proxy_async_smem();
+        named_bar(1, 128);
+        if (threadIdx.x == 384) mbar_arrive(&sm.k_ready[s]);
+      }
     }
   } else {
+    setmaxnreg_inc<kFwdRegsCompute>();
     // ------------------------------------------------------------ compute warpgroups
     const int cw = warp - 4;
     const int g = cw >> 2;                 // warpgroup = query tile of the pair
@@ -242,29 +355,50 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int r = wq * 32 + lane;          // query row in the tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const bool leader = threadIdx.x == 128 + 128 * g;
-    const int q0 = (2 * pr + g) * kTile;
-    const int qrow = q0 + r;
     const float c2 = prm.c2;
     const uint32_t tS = tmem + 256 * g + lane_off;
     const uint32_t tO = tmem + 256 * g + 128 + lane_off;
+    int tg0 = 0;   // key tiles this warpgroup processed in earlier units
+#ifdef FRSA_TRACE
+    int tr_i = 0;
+#define FWD_TR(ev, jj)                                                                   \
+  do {                                                                                   \
+    if (leader && blockIdx.x < 2048 && tr_i < 512) {                                     \
+      g_trace_it[blockIdx.x * 1024 + g * 512 + tr_i] = globaltimer();                    \
+      g_trace_fl[blockIdx.x * 1024 + g * 512 + tr_i] = (ev) | ((jj) << 8) | (x.nact << 16); \
+      ++tr_i;                                                                            \
+    }                                                                                    \
+  } while (0)
+#else
+#define FWD_TR(ev, jj) \
+  do {                 \
+  } while (0)
+#endif
 
-    if (g < nact) {
+#pragma unroll 1
+    for (int u = ubeg; u < uend; ++u) {
+      const FwdUnit x = fwd_unit(prm, u);
+      if (g >= x.nact) continue;
+      const int bh = x.bh;
+      const int q0 = (2 * x.pr + g) * kTile;
+      const int qrow = q0 + r;
       float m2 = -INFINITY, l = 0.f;
-      const bool row_valid = qrow < N;
       // A warp whose 32 query rows are all padding skips the softmax math: its
       // P rows only ever reach O rows that are not stored.
       const bool warp_active = (q0 + wq * 32) < N;
 
       FRSA_STAMP(3);
 
-      for (int j = 0; j < prm.nkv; ++j) {
+      for (int j = 0; j < nkv; ++j) {
+        const int tg = tg0 + j;
         const int kv0 = j * kTile;
         const int nvalid = min(kTile, N - kv0);
-        const int b = j % PB;
-        mbar_wait(&sm.s_full[g], j & 1, abort_flag);
-        // P buffer b was last read by the P V of tile j - PB.
-        if (j >= PB) mbar_wait(&sm.o_full[g][b], ((j - PB) / PB) & 1, abort_flag);
+        const int b = tg % PB;
+        mbar_wait(&sm.s_full[g], tg & 1, abort_flag);
+        // P buffer b was last read by the P V of tile tg - PB.
+        if (tg >= PB) mbar_wait(&sm.o_full[g][b], ((tg - PB) / PB) & 1, abort_flag);
         tc_fence_after();
+        FWD_TR(1, j);
         if (j < 12) FRSA_STAMP(8 + 2 * j);
         if (warp_active) {
           // pass 1: row max over the valid columns
@@ -276,10 +410,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_ld32(tS + h * 64 + 32, sv[1]);
             tmem_wait_ld();
 #pragma unroll
-            for (int u = 0; u < 2; ++u)
+            for (int uu = 0; uu < 2; ++uu)
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                if (h * 64 + u * 32 + i < nvalid) mx = fmaxf(mx, sv[u][i]);
+                if (h * 64 + uu * 32 + i < nvalid) mx = fmaxf(mx, sv[uu][i]);
           }
           // The exponent base m2 is raised only when a tile's maximum exceeds
           // it by more than kFwdSlack (log2 units; P stays <= 2^kFwdSlack):
@@ -291,7 +425,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const float alpha = ex2(m2 - m_new);   // 0 on the first tile
             l *= alpha;
             if (j > 0) {
-              const int pj = j - 1;
+              const int pj = tg - 1;
               mbar_wait(&sm.o_full[g][pj % PB], (pj / PB) & 1, abort_flag);
               tc_fence_after();
 #pragma unroll
@@ -320,32 +454,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_ld32(tS + h * 64 + 32, sv[1]);
             tmem_wait_ld();
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cbase = h * 64 + u * 32;
+            for (int uu = 0; uu < 2; ++uu) {
+              const int cbase = h * 64 + uu * 32;
               if (cbase + 32 <= nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                  sv[u][i] = ex2(fmaf(sv[u][i], c2, -m2));
-                  sum += sv[u][i];
+                  sv[uu][i] = ex2(fmaf(sv[uu][i], c2, -m2));
+                  sum += sv[uu][i];
                 }
               } else if (cbase < nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                  sv[u][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[u][i], c2, -m2)) : 0.f;
-                  sum += sv[u][i];
+                  sv[uu][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[uu][i], c2, -m2)) : 0.f;
+                  sum += sv[uu][i];
                 }
               } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sv[u][i] = 0.f;
+                for (int i = 0; i < 32; ++i) sv[uu][i] = 0.f;
               }
 #pragma unroll
               for (int g4 = 0; g4 < 4; ++g4) {
                 uint4 w;
-                w.x = Elt<T>::pack(sv[u][g4 * 8 + 0], sv[u][g4 * 8 + 1]);
-                w.y = Elt<T>::pack(sv[u][g4 * 8 + 2], sv[u][g4 * 8 + 3]);
-                w.z = Elt<T>::pack(sv[u][g4 * 8 + 4], sv[u][g4 * 8 + 5]);
-                w.w = Elt<T>::pack(sv[u][g4 * 8 + 6], sv[u][g4 * 8 + 7]);
-                sts_u4(pb0 + h * kChunkBytes + sw128_off(r, u * 4 + g4), w);
+                w.x = Elt<T>::pack(sv[uu][g4 * 8 + 0], sv[uu][g4 * 8 + 1]);
+                w.y = Elt<T>::pack(sv[uu][g4 * 8 + 2], sv[uu][g4 * 8 + 3]);
+                w.z = Elt<T>::pack(sv[uu][g4 * 8 + 4], sv[uu][g4 * 8 + 5]);
+                w.w = Elt<T>::pack(sv[uu][g4 * 8 + 6], sv[uu][g4 * 8 + 7]);
+                sts_u4(pb0 + h * kChunkBytes + sw128_off(r, uu * 4 + g4), w);
               }
             }
           }
@@ -355,6 +489,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_before();
         named_bar(2 + g, 128);
         if (leader) mbar_arrive(&sm.p_full[g]);
+        FWD_TR(2, j);
         if (j < 12) FRSA_STAMP(9 + 2 * j);
       }
       FRSA_STAMP(7);
@@ -362,14 +497,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // epilogue: lse = (m + log2 l) ln 2 and O / l, read from TMEM once the
       // last P V has completed and written through this group's first P
       // buffer (free) as an f32 staging area, one 64-column block at a time,
-      // by warp-per-row coalesced stores.
-      if (row_valid)
+      // by warp-per-row coalesced stores. The next unit's scores are already
+      // in flight meanwhile.
+      if (qrow < N)
         prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
       {
-        const int lj = prm.nkv - 1;
-        mbar_wait(&sm.o_full[g][lj % PB], (lj / PB) & 1, abort_flag);
+        const int lt = tg0 + nkv - 1;
+        mbar_wait(&sm.o_full[g][lt % PB], (lt / PB) & 1, abort_flag);
         tc_fence_after();
+        FWD_TR(3, 0);
       }
+      tg0 += nkv;
       const float inv_l = warp_active ? 1.f / l : 0.f;
       uint8_t* stage = &sm.p[g][0][0][0];
       T* o_head = reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D;
@@ -392,6 +530,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           named_bar(2 + g, 128);
         }
       }
+      // The O columns have been read: the next unit's first P V may
+      // overwrite them (it follows this group's next p_full arrival).
+      tc_fence_before();
+      FWD_TR(4, 0);
       FRSA_STAMP(30);
     }
   }
@@ -402,6 +544,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemColsFwd);
   }
+}
+
+// Guided schedule: one CTA per SM at a time (the shared-memory footprint
+// allows no second one), each CTA working a run of consecutive units so that
+// one unit's softmax tail and epilogue overlap the next unit's loads and
+// first scores. SMs do not run at the same speed (CTAs with identical work
+// finish up to 30 % apart on a B200), so the runs shrink from wave to wave:
+// wave w gives each of nsm CTAs about a 1/(2 nsm) share of the units still
+// left, and the last units go one per CTA. The hardware dispatches CTAs in
+// index order as SMs free up, which balances the tail dynamically without
+// any counter in global memory. Returns the grid size.
+int fwd_schedule(FwdParams& p, int nsm) {
+  const int nunits = p.nunits;
+  int rem = nunits, unit = 0, cta = 0, w = 0;
+  while (rem > 0 && w < kFwdMaxWaves - 1) {
+    const int c = rem / (2 * nsm);
+    if (c < 2) break;
+    p.wcta[w] = cta;
+    p.wunit[w] = unit;
+    p.wchunk[w] = c;
+    cta += nsm;
+    unit += nsm * c;
+    rem -= nsm * c;
+    ++w;
+  }
+  if (rem > 0) {   // (runs longer than 1 only for inputs beyond the wave limit)
+    const int c = rem / (8 * nsm) > 1 ? rem / (8 * nsm) : 1;
+    p.wcta[w] = cta;
+    p.wunit[w] = unit;
+    p.wchunk[w] = c;
+    cta += (rem + c - 1) / c;
+    ++w;
+  }
+  p.nwaves = w;
+  p.wcta[w] = cta;
+  return cta;
 }
 
 template <typename T, int NCH>
@@ -421,12 +599,16 @@ cudaError_t launch_fwd_t(const LaunchShape& s, const CUtensorMap& tm_q, const CU
   p.nkv = p.nqt;
   p.has_cls = s.has_cls;
   p.c2 = s.scale * 1.4426950408889634f;
+  const long long units = static_cast<long long>(s.BH) * p.npair;
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  p.nunits = static_cast<int>(units);
   const size_t smem = sizeof(FwdSmem<NCH>) + 1024;
   auto kern = fwd_kernel<T, NCH>;
   cudaError_t e = set_max_dynamic_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
-  const long long units = static_cast<long long>(s.BH) * p.npair;
-  kern<<<static_cast<unsigned>(units), kFwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, p);
+  if (p.nunits == 0) return cudaSuccess;
+  const int grid = fwd_schedule(p, device_sm_count());
+  kern<<<grid, kFwdThreads, smem, stream>>>(tm_q, tm_k, tm_v, p);
   return cudaGetLastError();
 }
 
