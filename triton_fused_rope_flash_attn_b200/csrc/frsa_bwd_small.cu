@@ -19,8 +19,10 @@
 // Warp roles (20 warps, 640 threads):
 //   warp 0        TMA producer (K, V, Q, dO tiles; the next head's tiles, O and
 //                 lse into L2)
-//   warp 1        TMEM allocator + MMA issuer
-//   warps 2..3    idle (complete warpgroup 0 for the register rebalancing)
+//   warp 1        TMEM allocator + MMA issuer of S^T and dV
+//   warp 2        MMA issuer of dP^T and dK
+//   warp 3        MMA issuer of dQ (one thread cannot issue the N = 64
+//                 products as fast as the tensor core runs them)
 //   warps 4..11   two elementwise warpgroups: warpgroup g computes P and dS for
 //                 query columns [64 g, 64 g + 64) of each iteration
 //   warps 12..15  rotation warpgroup: RoPE of the K and Q tiles in shared
@@ -194,8 +196,8 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
       mbar_init(&sm.k_ready[s], 1);
-      mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.dq_full[s], 1);
+      mbar_init(&sm.acc_full[s], 3);   // one commit per MMA issuer
+      mbar_init(&sm.dq_full[s], 3);
       mbar_init(&sm.dq_free[s], 1);
     }
     for (int s = 0; s < kQSlots; ++s) {
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.q_ready[s], 2);   // rotation group (Q^, lse2) + Delta group
     }
-    mbar_init(&sm.st_full, 1);
+    mbar_init(&sm.st_full, 3);
     mbar_init(&sm.ds_full, 1);
     mbar_init(&sm.acc_free, 1);
     fence_mbar_init();
@@ -263,35 +265,43 @@ __global__ void __launch_bounds__(kBsThreads, 1)
           tma_load_bh(sm.v[t], &tm_v, &sm.kv_full[t], 0, t * kTile, bh, prm.H);
         }
       }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
+    } else if (warp >= 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuers
+      // One thread issues tcgen05.mma at most about once per 90 cycles, well
+      // below the tensor core's rate for these N = 64 products, so three
+      // threads issue them: warp 1 S^T and dV, warp 2 dP^T and dK, warp 3
+      // dQ. Each keeps the order its operands need: S^T of iteration it + 1
+      // overwrites the P that dV of it reads (both warp 1), dP^T of it + 1
+      // the dS that dK of it reads (both warp 2). st_full, acc_full and
+      // dq_full take one commit from each issuer; warp 3's st_full commit
+      // after dQ of it tells the elementwise warps that the shared dS tile of
+      // it has been read.
+      const bool isA = warp == 1;
+      const bool isC = warp == 3;
       constexpr bool kBf = Elt<T>::kBf16;
       const uint32_t idKV = idesc_f16(kBf, 128, DP, false, true);    // dV, dK^
       const uint32_t idQ = idesc_f16(kBf, 128, DP, true, true);      // dQ^
       auto issue_st = [&](int it) __attribute__((always_inline)) {
+        if (isC) return;
         const int hl = it / per_head, w = it - hl * per_head;
         const int j = w / nqt, i = w - j * nqt;
         const int u = hl * nqt + i, sl = qslot(u);
         mbar_wait(&sm.k_ready[j], hl & 1, abort_flag);
         mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);
         tc_fence_after();
-        if (it >= 5 && it < 9) FRSA_STAMP_T(49 + 2 * (it - 5), 32);
-        // S^T, dP^T: only the query columns that hold tokens (rounded up to 16).
+        // S^T (warp 1) or dP^T (warp 2): only the query columns that hold
+        // tokens (rounded up to 16).
         const uint32_t idS = idesc_f16(kBf, 128, 16 * valid16(i), false, false);
+        const uint32_t dst = isA ? tST : tDPT;
+        const uint32_t a0 = smem_u32(isA ? sm.k[j] : sm.v[j]);
+        const uint32_t b0 = smem_u32(isA ? sm.q[sl] : sm.dO[sl]);
 #pragma unroll 1
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t koff = kk * 32;
-          mma_ss(tST, sw128_desc(smem_u32(sm.k[j]) + koff, 16, 1024),
-                 sw128_desc(smem_u32(sm.q[sl]) + koff, 16, 1024), idS, kk > 0);
-        }
-#pragma unroll 1
-        for (int kk = 0; kk < ksteps; ++kk) {
-          const uint32_t koff = kk * 32;
-          mma_ss(tDPT, sw128_desc(smem_u32(sm.v[j]) + koff, 16, 1024),
-                 sw128_desc(smem_u32(sm.dO[sl]) + koff, 16, 1024), idS, kk > 0);
+          mma_ss(dst, sw128_desc(a0 + koff, 16, 1024), sw128_desc(b0 + koff, 16, 1024), idS, kk > 0);
         }
         mma_commit(&sm.st_full);
-        if (it >= 4 && it < 12) FRSA_STAMP_T(16 + it - 4, 32);
+        if (isA && it >= 4 && it < 12) FRSA_STAMP_T(16 + it - 4, 32);
       };
       auto issue_grads = [&](int it) __attribute__((always_inline)) {
         const int hl = it / per_head, w = it - hl * per_head;
@@ -300,49 +310,52 @@ __global__ void __launch_bounds__(kBsThreads, 1)
         mbar_wait(&sm.ds_full, it & 1, abort_flag);
         tc_fence_after();
         const int kvt = hl * nkv + j;   // running key-tile index
-        if (i == 0 && kvt > 0) {
+        if (!isC && i == 0 && kvt > 0) {
           mbar_wait(&sm.acc_free, (kvt - 1) & 1, abort_flag);   // dV/dK of the previous tile drained
           tc_fence_after();
         }
-        if (j == 0 && hl > 0) {
+        if (isC && j == 0 && hl > 0) {
           mbar_wait(&sm.dq_free[i], (hl - 1) & 1, abort_flag);  // previous head's dQ_i drained
           tc_fence_after();
         }
-        if (it >= 4 && it < 12) FRSA_STAMP_T(24 + it - 4, 32);
+        if (isA && it >= 4 && it < 12) FRSA_STAMP_T(24 + it - 4, 32);
         const int kq = valid16(i), kkeys = valid16(j);
-#pragma unroll 1
-        for (int kk = 0; kk < kq; ++kk) {
-          // Query columns [16 kk, 16 kk + 16) of P / dS: packed TMEM columns
+        if (!isC) {
+          // dV += P dO (warp 1) or dK^ += dS Q^ (warp 2): A = P or dS
+          // [key][query] in TMEM, B = dO or Q^ [query][d] MN-major. Query
+          // columns [16 kk, 16 kk + 16) of P / dS sit in packed TMEM columns
           // 64 (kk / 4) + 8 (kk % 4).
-          const uint32_t pcol = 64 * (kk >> 2) + 8 * (kk & 3);
-          const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-          // dV += P dO : A = P [key][query] in TMEM, B = dO [query][d] MN-major.
-          mma_ts(tDV, tST + pcol, sw128_desc(smem_u32(sm.dO[sl]) + kk * 2048, kChunkBytes, 1024),
-                 idKV, acc);
-          // dK^ += dS Q^ : A = dS [key][query] in TMEM, B = Q^ [query][d] MN-major.
-          mma_ts(tDK, tDPT + pcol, sw128_desc(smem_u32(sm.q[sl]) + kk * 2048, kChunkBytes, 1024),
-                 idKV, acc);
-        }
-        // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d]
-        // MN-major. Query rows past the computed columns read stale dS; they
-        // only reach dQ rows past N, which are never stored.
+          const uint32_t dacc = isA ? tDV : tDK;
+          const uint32_t asrc = isA ? tST : tDPT;
+          const uint32_t b0 = smem_u32(isA ? sm.dO[sl] : sm.q[sl]);
 #pragma unroll 1
-        for (int kk = 0; kk < kkeys; ++kk) {
-          const uint32_t acc = (j == 0 && kk == 0) ? 0u : 1u;
-          mma_ss(tmem + 384 + 64 * i, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
-                 sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
+          for (int kk = 0; kk < kq; ++kk) {
+            const uint32_t pcol = 64 * (kk >> 2) + 8 * (kk & 3);
+            const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
+            mma_ts(dacc, asrc + pcol, sw128_desc(b0 + kk * 2048, kChunkBytes, 1024), idKV, acc);
+          }
+        } else {
+          // dQ^_i (+)= dS^T K^ : A = dS read query-major (MN-major), B = K^
+          // [key][d] MN-major. Query rows past the computed columns read
+          // stale dS; they only reach dQ rows past N, which are never stored.
+#pragma unroll 1
+          for (int kk = 0; kk < kkeys; ++kk) {
+            const uint32_t acc = (j == 0 && kk == 0) ? 0u : 1u;
+            mma_ss(tmem + 384 + 64 * i, sw128_desc(smem_u32(sm.ds[0]) + kk * 2048, kChunkBytes, 1024),
+                   sw128_desc(smem_u32(sm.k[j]) + kk * 2048, kChunkBytes, 1024), idQ, acc);
+          }
+          mma_commit(&sm.st_full);   // dS of iteration it read (phase it + 1)
         }
-        if (it >= 4 && it < 8) FRSA_STAMP_T(48 + 2 * (it - 4), 32);
+        if (isA && it >= 4 && it < 8) FRSA_STAMP_T(48 + 2 * (it - 4), 32);
         // K_j/V_j and the query slot are released by the aux warpgroup once it
         // has staged the finished gradients in them and their stores have read them.
         if (i == nqt - 1) mma_commit(&sm.acc_full[j]);
         if (j == nkv - 1) mma_commit(&sm.dq_full[i]);
       };
       // S^T/dP^T of iteration it + 1 overwrite P/dS of iteration it in TMEM,
-      // so they follow its gradient products in the (in-order) MMA pipe; their
-      // completion (st_full) also tells the elementwise warps that the dQ
-      // product has read the shared dS tile.
-      // (One call site each keeps this warp's code small.)
+      // so they follow its gradient products in each issuer's (in-order)
+      // stream. (One call site each keeps this code small.)
+      if (isC) mma_commit(&sm.st_full);   // phase 0 has no dQ before it
       for (int it = 0; it <= total; ++it) {
         if (it > 0) issue_grads(it - 1);
         if (it < total) issue_st(it);
@@ -359,13 +372,31 @@ __global__ void __launch_bounds__(kBsThreads, 1)
     const bool leader = threadIdx.x == 128;
     const float c2 = prm.c2;
     const uint32_t dbase = smem_u32(sm.ds[g]);
+#ifdef FRSA_TRACE
+    int tr_i = 0;
+#define BS_TR(ev)                                                                   \
+  do {                                                                              \
+    if ((threadIdx.x & 127) == 0 && blockIdx.x < 2048 && tr_i < 512) {              \
+      g_trace_it[blockIdx.x * 1024 + g * 512 + tr_i] = globaltimer();               \
+      g_trace_fl[blockIdx.x * 1024 + g * 512 + tr_i] = (ev);                        \
+      ++tr_i;                                                                       \
+    }                                                                               \
+  } while (0)
+#else
+#define BS_TR(ev) \
+  do {            \
+  } while (0)
+#endif
     for (int it = 0; it < total; ++it) {
       const int hl = it / per_head, w = it - hl * per_head;
       const int i = w - (w / nqt) * nqt;
       const int u = hl * nqt + i, sl = qslot(u);
+      BS_TR(0);
       mbar_wait(&sm.q_ready[sl], qphase(u), abort_flag);   // lse2 / Delta of this query tile
+      BS_TR(1);
       mbar_wait(&sm.st_full, it & 1, abort_flag);
       tc_fence_after();
+      BS_TR(2);
       if (it >= 4 && it < 12) FRSA_STAMP_T(2 * (it - 4), 128);
       const uint32_t lbase = smem_u32(&sm.lse2[u & 1][g * 64]);
       const uint32_t ebase = smem_u32(&sm.delta[u & 1][g * 64]);
@@ -405,6 +436,7 @@ __global__ void __launch_bounds__(kBsThreads, 1)
       tc_fence_before();
       named_bar(1, 256);
       if (leader) mbar_arrive(&sm.ds_full);
+      BS_TR(3);
       if (it >= 4 && it < 12) FRSA_STAMP_T(2 * (it - 4) + 1, 128);
     }
   } else {

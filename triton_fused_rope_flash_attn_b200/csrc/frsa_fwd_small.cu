@@ -38,6 +38,10 @@ namespace {
 
 constexpr int kFsThreads = 512;
 constexpr int kFsRotThreads = 192;   // warps 2-3 and 12-15
+// Registers per thread after the per-warpgroup split (launch: 128 each, 512
+// threads): warpgroups 0 and 3 (producer, MMA, rotation) 88, the two softmax
+// warpgroups 168: 88 + 88 + 2 x 168 = 4 x 128.
+constexpr uint32_t kFsRegsAux = 88, kFsRegsSoft = 168;
 
 struct FsSmem {
   uint8_t q[2][2][kChunkBytes];    // [head stage][query tile]
@@ -110,6 +114,8 @@ __global__ void __launch_bounds__(kFsThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  if (warp < 4 || warp >= 12) {
+  setmaxnreg_dec<kFsRegsAux>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -212,7 +218,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       }
       if (nqt > 1 && hl > 0) issue_pv(1, hl - 1);
     }
-  } else if (warp < 4 || warp >= 12) {
+  } else {
     // ------------------------------------------------------------ rotation warps
     // 192 threads; thread t rotates token rows t, t + 192, ... of a stage.
     const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 320;
@@ -240,7 +246,9 @@ __global__ void __launch_bounds__(kFsThreads, 1)
       named_bar(1, kFsRotThreads);
       if (t == 0) mbar_arrive(&sm.k_ready[st]);
     }
+  }
   } else {
+    setmaxnreg_inc<kFsRegsSoft>();
     // ------------------------------------------------------------ softmax warpgroups
     // One pass per head: the whole score row is in TMEM, so the maximum is
     // exact and nothing is rescaled.
@@ -258,14 +266,32 @@ __global__ void __launch_bounds__(kFsThreads, 1)
     // A warp whose 32 query rows are all padding skips the softmax math: its P
     // rows only ever reach O rows that are not stored.
     const bool warp_active = (q0 + wq * 32) < N;
+#ifdef FRSA_TRACE
+    int tr_i = 0;
+    const bool tr_lead = (threadIdx.x & 127) == 0;
+#define FS_TR(ev)                                                                   \
+  do {                                                                              \
+    if (tr_lead && blockIdx.x < 2048 && tr_i < 512) {                               \
+      g_trace_it[blockIdx.x * 1024 + g * 512 + tr_i] = globaltimer();               \
+      g_trace_fl[blockIdx.x * 1024 + g * 512 + tr_i] = (ev);                        \
+      ++tr_i;                                                                       \
+    }                                                                               \
+  } while (0)
+#else
+#define FS_TR(ev) \
+  do {            \
+  } while (0)
+#endif
     if (g < nqt) {
       int hl = 0;
       for (int bh = blockIdx.x; bh < prm.BH; bh += gridDim.x, ++hl) {
+        FS_TR(0);
         mbar_wait(&sm.s_full[g], hl & 1, abort_flag);
         tc_fence_after();
+        FS_TR(1);
         float m2 = 0.f, l = 1.f;
         if (warp_active) {
-          float mx = -INFINITY;
+          float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
           for (int h = 0; h < npair; ++h) {
             float sv[2][32];
@@ -277,16 +303,17 @@ __global__ void __launch_bounds__(kFsThreads, 1)
               const int cbase = h * 64 + u * 32;
               if (cbase + 32 <= N) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[u][i]);
+                for (int i = 0; i < 32; ++i) mxp[i & 3] = fmaxf(mxp[i & 3], sv[u][i]);
               } else {
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                  if (cbase + i < N) mx = fmaxf(mx, sv[u][i]);
+                  if (cbase + i < N) mxp[i & 3] = fmaxf(mxp[i & 3], sv[u][i]);
               }
             }
           }
-          m2 = mx * c2;
-          float sum = 0.f;
+          m2 = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])) * c2;
+          FS_TR(2);
+          float sp[4] = {0.f, 0.f, 0.f, 0.f};
           // Split: the 64-key steps past key 128 go first and their P goes to
           // columns [nk16, ...), past the scores, so P V can start on them
           // while keys [0, 128) are processed (then published by p_full).
@@ -307,7 +334,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
                 for (int i = 0; i < 16; ++i) {
                   const float a = ex2(fmaf(sv[u][2 * i], c2, -m2));
                   const float b = ex2(fmaf(sv[u][2 * i + 1], c2, -m2));
-                  sum += a + b;
+                  sp[i & 3] += a + b;
                   pk[i] = Elt<T>::pack(a, b);
                 }
               } else {
@@ -316,7 +343,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
                   const float a = (cbase + 2 * i < N) ? ex2(fmaf(sv[u][2 * i], c2, -m2)) : 0.f;
                   const float b =
                       (cbase + 2 * i + 1 < N) ? ex2(fmaf(sv[u][2 * i + 1], c2, -m2)) : 0.f;
-                  sum += a + b;
+                  sp[i & 3] += a + b;
                   pk[i] = Elt<T>::pack(a, b);
                 }
               }
@@ -334,7 +361,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
             }
           }
           tmem_wait_st();
-          l = sum;
+          l = (sp[0] + sp[1]) + (sp[2] + sp[3]);
         } else if (split) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.p_hi[g]);
@@ -343,11 +370,13 @@ __global__ void __launch_bounds__(kFsThreads, 1)
         // Each warp publishes its own rows (no cross-warp barrier here).
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_full[g]);
+        FS_TR(3);
 
         if (qrow < N)
           prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
         mbar_wait(&sm.o_full[g], hl & 1, abort_flag);
         tc_fence_after();
+        FS_TR(4);
         // Epilogue: O / l as 16-bit rows, stored straight from registers
         // (each thread writes its whole 2 D-byte row).
         if (warp_active) {
@@ -376,6 +405,7 @@ __global__ void __launch_bounds__(kFsThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.o_free[g]);
+        FS_TR(5);
       }
     }
   }
