@@ -17,18 +17,18 @@
 //   warps 12..15  rotation warps: apply RoPE in shared memory to the Q
 //               tiles and to every K tile as soon as TMA has landed it
 //   warps 4..11 two compute warpgroups, warpgroup g owns query tile g of the
-//               pair: it reads S from TMEM (thread = query row), writes P
-//               (16-bit) to its shared P buffers (two when D <= 64, so the
-//               next tile's softmax does not wait for this tile's P V), and
+//               pair: it reads S from TMEM (thread = query row), writes P as
+//               packed 16-bit pairs back over the scores it has read, and
 //               writes O and the log-sum-exp. O accumulates in TMEM; the
 //               softmax base is raised (and O rescaled in TMEM) only when a
-//               tile's maximum exceeds it by more than 2^8. The MMA issue
-//               order (S_0 next, P_0 V, S_1 next, P_1 V) lets the two groups
-//               run out of phase and each group's next softmax overlap its
-//               own P V.
+//               tile's maximum exceeds it by more than 2^8. P V reads P from
+//               TMEM (A operand) and V from shared memory, so P never touches
+//               shared memory. The MMA issue order (P_0 V, S_0 next, P_1 V,
+//               S_1 next) lets one group's products run while the other
+//               group is in its softmax.
 //
-// TMEM columns: warpgroup g uses [256 g, 256 g + 128) for S and
-// [256 g + 128, 256 g + 128 + DP) for O.
+// TMEM columns: warpgroup g uses [256 g, 256 g + 128) for S (P packed in
+// the first 64) and [256 g + 128, 256 g + 128 + DP) for O.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
 #include "frsa_rope.cuh"
@@ -51,18 +51,18 @@ constexpr int kFwdMaxWaves = 12;   // chunk-size levels of the guided schedule  
 
 template <int NCH>
 struct FwdSmem {
-  static constexpr int KS = (NCH == 1) ? 2 : 1;  // K and V ring stages
-  static constexpr int PB = (NCH == 1) ? 2 : 1;  // P buffers per warpgroup
+  // K and V ring stages: the P tiles live in TMEM, so shared memory holds
+  // only the two query tiles and the K/V ring.
+  static constexpr int KS = (NCH == 1) ? 4 : 2;
   uint8_t q[2][NCH][kChunkBytes];      // query tile of warpgroup g
   uint8_t k[KS][NCH][kChunkBytes];     // key ring
   uint8_t v[KS][NCH][kChunkBytes];     // value ring
-  uint8_t p[2][PB][2][kChunkBytes];    // P tiles of warpgroup g: [128 q][128 kv], two chunks
   uint64_t q_full[2], q_ready[2], q_empty[2];
   uint64_t k_full[KS], k_ready[KS], k_empty[KS];
   uint64_t v_full[KS], v_empty[KS];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_full[2][PB];              // P V of a tile using P buffer b has completed
+  uint64_t o_full[2];                  // the last P V of a unit has completed
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -110,7 +110,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
   using Sm = FwdSmem<NCH>;
   constexpr int KS = Sm::KS;
-  constexpr int PB = Sm::PB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Sm* smp = aligned_smem<Sm>(smem_raw);
   if (smp == nullptr) return;
@@ -134,7 +133,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
       mbar_init(&sm.p_full[s], 1);
-      for (int b = 0; b < Sm::PB; ++b) mbar_init(&sm.o_full[s][b], 1);
+      mbar_init(&sm.o_full[s], 1);
     }
     for (int s = 0; s < KS; ++s) {
       mbar_init(&sm.k_full[s], 1);
@@ -158,8 +157,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // Barrier phases. Query-tile buffer g is filled once per unit in which
   // query tile g of the pair exists (fill f: parity f & 1); the K/V tiles
   // form one running sequence t over the CTA's units (stage t % KS, parity
-  // (t / KS) & 1); warpgroup g's S / P / O barriers count the key tiles it
-  // has processed.
+  // (t / KS) & 1); warpgroup g's S and P barriers count the key tiles it has
+  // processed, its O barrier the units.
   if (warp < 4) {
   setmaxnreg_dec<kFwdRegsCtl>();
   if (warp == 0) {
@@ -211,16 +210,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(&sm.s_full[g]);
       };
-      // O_g (+)= P_g V : A = P [q][kv] K-major, B = V [kv][d] MN-major. O
-      // accumulates over the key tiles of a unit in TMEM.
-      auto issue_pv = [&](int g, int s, int b, bool acc) {
-        const uint32_t tO = tmem + 256 * g + 128;
-        for (int ks = 0; ks < kTile / 16; ++ks) {
-          mma_ss(tO, sw128_desc(smem_u32(sm.p[g][b][ks >> 2]) + (ks & 3) * 32, 16, 1024),
-                 sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024), idO,
-                 acc || ks > 0);
-        }
-        mma_commit(&sm.o_full[g][b]);
+      // O_g (+)= P_g V : A = P [q][kv] from TMEM (packed 16-bit pairs over
+      // the scores: keys [16 ks, 16 ks + 16) in columns [8 ks, 8 ks + 8)),
+      // B = V [kv][d] MN-major. O accumulates over a unit's key tiles.
+      auto issue_pv = [&](int g, int s, bool acc) {
+        const uint32_t tS = tmem + 256 * g;
+        const uint32_t tO = tS + 128;
+        for (int ks = 0; ks < kTile / 16; ++ks)
+          mma_ts(tO, tS + 8 * ks, sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024),
+                 idO, acc || ks > 0);
       };
       int qf[2] = {0, 0};   // query-tile fill of the current unit, per warpgroup
       int tg[2] = {0, 0};   // key tiles processed, per warpgroup
@@ -246,57 +244,47 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int t1 = t + 1, s1 = t1 % KS;
           bool k_waited = false, v_waited = false;
           bool any_s = false;
-          auto wait_v = [&]() {
-            if (!v_waited) {
-              mbar_wait(&sm.v_full[s], (t / KS) & 1, abort_flag);
-              tc_fence_after();
-              v_waited = true;
-            }
-          };
           auto wait_k = [&]() {
             if (!k_waited) {
               mbar_wait(&sm.k_ready[s1], (t1 / KS) & 1, abort_flag);
               k_waited = true;
             }
           };
-          if (more) {
-            // S_g of the next key tile goes ahead of P_g V of this tile: P is
-            // in shared memory, so S may overwrite the scores as soon as the
-            // softmax has published P, and the group's next softmax overlaps
-            // this P V.
-            for (int g = 0; g < x.nact; ++g) {
-              mbar_wait(&sm.p_full[g], tg[g] & 1, abort_flag);
-              tc_fence_after();
+          // Per group: P_g V of this key tile, then (P overwritten only
+          // after the P V that reads it, by this thread's in-order issue)
+          // S_g of the next key tile. The two groups alternate, so the
+          // tensor core works on one group's products while the other group
+          // is in its softmax.
+          for (int g = 0; g < x.nact; ++g) {
+            mbar_wait(&sm.p_full[g], tg[g] & 1, abort_flag);
+            if (!v_waited) {
+              mbar_wait(&sm.v_full[s], (t / KS) & 1, abort_flag);
+              v_waited = true;
+            }
+            tc_fence_after();
+            issue_pv(g, s, j > 0);
+            ++tg[g];
+            if (!more) {
+              mma_commit(&sm.o_full[g]);
+            } else {
               wait_k();
               tc_fence_after();
               issue_s(g, s1);
               // The last score product of a query tile frees its buffer.
               if (j + 2 == nkv) mma_commit(&sm.q_empty[g]);
               any_s = true;
-              wait_v();
-              issue_pv(g, s, tg[g] % PB, j > 0);
-              ++tg[g];
             }
-          } else {
-            // Last key tile of the unit: its P V products go first, so that
-            // the epilogue never waits for the next unit's query tiles to
-            // land and rotate; then the next unit's first scores.
-            for (int g = 0; g < x.nact; ++g) {
-              mbar_wait(&sm.p_full[g], tg[g] & 1, abort_flag);
+          }
+          if (!more && has_next) {
+            // The next unit's first scores (its query tiles have landed and
+            // rotated meanwhile).
+            for (int g = 0; g < xn.nact; ++g) {
+              wait_k();
+              mbar_wait(&sm.q_ready[g], (qf[g] + (g < x.nact ? 1 : 0)) & 1, abort_flag);
               tc_fence_after();
-              wait_v();
-              issue_pv(g, s, tg[g] % PB, j > 0);
-              ++tg[g];
-            }
-            if (has_next) {
-              for (int g = 0; g < xn.nact; ++g) {
-                wait_k();
-                mbar_wait(&sm.q_ready[g], (qf[g] + (g < x.nact ? 1 : 0)) & 1, abort_flag);
-                tc_fence_after();
-                issue_s(g, s1);
-                if (nkv == 1) mma_commit(&sm.q_empty[g]);
-                any_s = true;
-              }
+              issue_s(g, s1);
+              if (nkv == 1) mma_commit(&sm.q_empty[g]);
+              any_s = true;
             }
           }
           if (any_s) mma_commit(&sm.k_empty[s1]);
@@ -359,6 +347,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tS = tmem + 256 * g + lane_off;
     const uint32_t tO = tmem + 256 * g + 128 + lane_off;
     int tg0 = 0;   // key tiles this warpgroup processed in earlier units
+    int uo = 0;    // units this warpgroup finished (o_full phase)
 #ifdef FRSA_TRACE
     int tr_i = 0;
 #define FWD_TR(ev, jj)                                                                   \
@@ -387,22 +376,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // P rows only ever reach O rows that are not stored.
       const bool warp_active = (q0 + wq * 32) < N;
 
-      FRSA_STAMP(3);
-
       for (int j = 0; j < nkv; ++j) {
         const int tg = tg0 + j;
-        const int kv0 = j * kTile;
-        const int nvalid = min(kTile, N - kv0);
-        const int b = tg % PB;
+        const int nvalid = min(kTile, N - j * kTile);
+        FWD_TR(0, j);
+        // S of tile tg has landed; its commit also orders the P V of tile
+        // tg - 1 (issued before it), so P and O are free to touch.
         mbar_wait(&sm.s_full[g], tg & 1, abort_flag);
-        // P buffer b was last read by the P V of tile tg - PB.
-        if (tg >= PB) mbar_wait(&sm.o_full[g][b], ((tg - PB) / PB) & 1, abort_flag);
         tc_fence_after();
         FWD_TR(1, j);
-        if (j < 12) FRSA_STAMP(8 + 2 * j);
         if (warp_active) {
-          // pass 1: row max over the valid columns
-          float mx = -INFINITY;
+          // pass 1: row max over the valid columns (eight independent chains)
+          float mxp[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float sv[2][32];
@@ -410,24 +397,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_ld32(tS + h * 64 + 32, sv[1]);
             tmem_wait_ld();
 #pragma unroll
-            for (int uu = 0; uu < 2; ++uu)
+            for (int uu = 0; uu < 2; ++uu) {
+              if (h * 64 + uu * 32 + 32 <= nvalid) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (h * 64 + uu * 32 + i < nvalid) mx = fmaxf(mx, sv[uu][i]);
+                for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], sv[uu][i]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (h * 64 + uu * 32 + i < nvalid) mxp[i & 7] = fmaxf(mxp[i & 7], sv[uu][i]);
+              }
+            }
           }
+          const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                 fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
           // The exponent base m2 is raised only when a tile's maximum exceeds
           // it by more than kFwdSlack (log2 units; P stays <= 2^kFwdSlack):
-          // then l and the O accumulated in TMEM so far are rescaled, after
-          // the previous P V has completed.
+          // then l and the O accumulated in TMEM so far are rescaled.
           const bool up = mx * c2 > m2 + kFwdSlack;
           if (__any_sync(0xffffffffu, up)) {
             const float m_new = up ? mx * c2 : m2;
             const float alpha = ex2(m2 - m_new);   // 0 on the first tile
             l *= alpha;
             if (j > 0) {
-              const int pj = tg - 1;
-              mbar_wait(&sm.o_full[g][pj % PB], (pj / PB) & 1, abort_flag);
-              tc_fence_after();
 #pragma unroll
               for (int c16 = 0; c16 < 4 * NCH; ++c16) {
                 if (c16 * 16 < DP) {
@@ -440,13 +431,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   tmem_st16(tO + c16 * 16, w);
                 }
               }
-              tmem_wait_st();
             }
             m2 = m_new;
           }
-          // pass 2: P = exp2(S c2 - m2), row sum, 16-bit P into buffer b
-          float sum = 0.f;
-          const uint32_t pb0 = smem_u32(sm.p[g][b][0]);
+          // pass 2: P = exp2(S c2 - m2), row sum; 16-bit P packed in pairs
+          // into TMEM columns [32 h, 32 h + 32) for the keys [64 h, 64 h + 64)
+          // (columns this thread has already read: the write front trails
+          // the read front).
+          float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float sv[2][32];
@@ -456,85 +448,81 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int uu = 0; uu < 2; ++uu) {
               const int cbase = h * 64 + uu * 32;
+              uint32_t pk[16];
               if (cbase + 32 <= nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                   sv[uu][i] = ex2(fmaf(sv[uu][i], c2, -m2));
-                  sum += sv[uu][i];
+                  sp[i & 3] += sv[uu][i];
                 }
               } else if (cbase < nvalid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                   sv[uu][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[uu][i], c2, -m2)) : 0.f;
-                  sum += sv[uu][i];
+                  sp[i & 3] += sv[uu][i];
                 }
               } else {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) sv[uu][i] = 0.f;
               }
 #pragma unroll
-              for (int g4 = 0; g4 < 4; ++g4) {
-                uint4 w;
-                w.x = Elt<T>::pack(sv[uu][g4 * 8 + 0], sv[uu][g4 * 8 + 1]);
-                w.y = Elt<T>::pack(sv[uu][g4 * 8 + 2], sv[uu][g4 * 8 + 3]);
-                w.z = Elt<T>::pack(sv[uu][g4 * 8 + 4], sv[uu][g4 * 8 + 5]);
-                w.w = Elt<T>::pack(sv[uu][g4 * 8 + 6], sv[uu][g4 * 8 + 7]);
-                sts_u4(pb0 + h * kChunkBytes + sw128_off(r, uu * 4 + g4), w);
-              }
+              for (int i = 0; i < 16; ++i) pk[i] = Elt<T>::pack(sv[uu][2 * i], sv[uu][2 * i + 1]);
+              tmem_st16(tS + h * 32 + uu * 16, pk);
             }
           }
-          l += sum;
+          l += (sp[0] + sp[1]) + (sp[2] + sp[3]);
+          tmem_wait_st();
         }
-        fence_proxy_async_smem();
         tc_fence_before();
         named_bar(2 + g, 128);
         if (leader) mbar_arrive(&sm.p_full[g]);
         FWD_TR(2, j);
-        if (j < 12) FRSA_STAMP(9 + 2 * j);
       }
-      FRSA_STAMP(7);
 
       // epilogue: lse = (m + log2 l) ln 2 and O / l, read from TMEM once the
-      // last P V has completed and written through this group's first P
-      // buffer (free) as an f32 staging area, one 64-column block at a time,
-      // by warp-per-row coalesced stores. The next unit's scores are already
-      // in flight meanwhile.
+      // unit's last P V has completed and stored from registers (thread =
+      // query row). The next unit's scores are already in flight meanwhile.
       if (qrow < N)
         prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
-      {
-        const int lt = tg0 + nkv - 1;
-        mbar_wait(&sm.o_full[g][lt % PB], (lt / PB) & 1, abort_flag);
-        tc_fence_after();
-        FWD_TR(3, 0);
-      }
+      mbar_wait(&sm.o_full[g], uo & 1, abort_flag);
+      tc_fence_after();
+      FWD_TR(3, 0);
+      ++uo;
       tg0 += nkv;
-      const float inv_l = warp_active ? 1.f / l : 0.f;
-      uint8_t* stage = &sm.p[g][0][0][0];
-      T* o_head = reinterpret_cast<T*>(prm.o) + static_cast<size_t>(bh) * N * D;
+      // (tcgen05.ld is warp-collective: the loads run in every lane of an
+      // active warp, the stores only for rows that hold tokens)
+      if (warp_active) {
+        const float inv_l = 1.f / l;
+        uint4* orow = reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.o) +
+                                               (static_cast<size_t>(bh) * N + qrow) * D);
 #pragma unroll
-      for (int blk = 0; blk < NCH; ++blk) {
-        if (blk * 64 < D) {
-#pragma unroll
-          for (int c16 = 0; c16 < 4; ++c16) {
+        for (int c16 = 0; c16 < 8; ++c16) {
+          if (c16 * 16 < DP) {
             float v[16];
-            if (warp_active) {
-              tmem_ld16(tO + blk * 64 + c16 * 16, v);
-              tmem_wait_ld();
-            }
+            tmem_ld16(tO + c16 * 16, v);
+            tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = warp_active ? v[e] * inv_l : 0.f;
-            stage_write16<1>(stage, r, c16, v);
+            for (int e = 0; e < 16; ++e) v[e] *= inv_l;
+            uint4 w0, w1;
+            w0.x = Elt<T>::pack(v[0], v[1]);
+            w0.y = Elt<T>::pack(v[2], v[3]);
+            w0.z = Elt<T>::pack(v[4], v[5]);
+            w0.w = Elt<T>::pack(v[6], v[7]);
+            w1.x = Elt<T>::pack(v[8], v[9]);
+            w1.y = Elt<T>::pack(v[10], v[11]);
+            w1.z = Elt<T>::pack(v[12], v[13]);
+            w1.w = Elt<T>::pack(v[14], v[15]);
+            if (qrow < N) {
+              orow[2 * c16] = w0;
+              if (c16 * 16 + 8 < D) orow[2 * c16 + 1] = w1;
+            }
           }
-          named_bar(2 + g, 128);
-          drain_block_q<T, 32>(stage, wq * 32, q0, N, D, blk, o_head, lane);
-          named_bar(2 + g, 128);
         }
       }
       // The O columns have been read: the next unit's first P V may
       // overwrite them (it follows this group's next p_full arrival).
       tc_fence_before();
       FWD_TR(4, 0);
-      FRSA_STAMP(30);
     }
   }
 
