@@ -386,84 +386,99 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         FWD_TR(1, j);
         if (warp_active) {
-          // pass 1: row max over the valid columns (eight independent chains)
-          float mxp[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
-#pragma unroll
+          // One pass over the scores, 64 columns at a time: the half's row
+          // maximum, then P = exp2(S c2 - m2) and the row sum; 16-bit P is
+          // packed in pairs into TMEM columns [32 h, 32 h + 32) for the keys
+          // [64 h, 64 h + 64) (columns this thread has already read: the
+          // write front trails the read front). The exponent base m2 is
+          // raised only when a half's maximum exceeds it by more than
+          // kFwdSlack (log2 units; P stays <= 2^kFwdSlack): then l, the
+          // partial sums, the O accumulated in TMEM so far (the previous
+          // tile's P V has completed: the commit of this tile's S follows
+          // it) and, for the second half, the first half's P are rescaled.
+          float sp[4] = {0.f, 0.f, 0.f, 0.f};
+          // (not unrolled: one copy of the body, with its rarely taken
+          // rescale code, keeps the loop small in the instruction cache)
+#pragma unroll 1
           for (int h = 0; h < 2; ++h) {
+            if (h * 64 >= nvalid) {   // only padding keys: P = 0
+              uint32_t z[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) z[i] = 0u;
+              tmem_st16(tS + h * 32, z);
+              tmem_st16(tS + h * 32 + 16, z);
+              continue;
+            }
             float sv[2][32];
             tmem_ld32(tS + h * 64, sv[0]);
             tmem_ld32(tS + h * 64 + 32, sv[1]);
             tmem_wait_ld();
+            if (h * 64 + 64 > nvalid) {
 #pragma unroll
-            for (int uu = 0; uu < 2; ++uu) {
-              if (h * 64 + uu * 32 + 32 <= nvalid) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], sv[uu][i]);
-              } else {
+              for (int uu = 0; uu < 2; ++uu)
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                  if (h * 64 + uu * 32 + i < nvalid) mxp[i & 7] = fmaxf(mxp[i & 7], sv[uu][i]);
-              }
+                  if (h * 64 + uu * 32 + i >= nvalid) sv[uu][i] = -INFINITY;
             }
-          }
-          const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                 fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-          // The exponent base m2 is raised only when a tile's maximum exceeds
-          // it by more than kFwdSlack (log2 units; P stays <= 2^kFwdSlack):
-          // then l and the O accumulated in TMEM so far are rescaled.
-          const bool up = mx * c2 > m2 + kFwdSlack;
-          if (__any_sync(0xffffffffu, up)) {
-            const float m_new = up ? mx * c2 : m2;
-            const float alpha = ex2(m2 - m_new);   // 0 on the first tile
-            l *= alpha;
-            if (j > 0) {
+            float mxp[8];
 #pragma unroll
-              for (int c16 = 0; c16 < 4 * NCH; ++c16) {
-                if (c16 * 16 < DP) {
-                  float ov[16];
-                  tmem_ld16(tO + c16 * 16, ov);
+            for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(sv[0][i], sv[0][i + 8]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              mxp[i] = fmaxf(fmaxf(mxp[i], sv[0][i + 16]), sv[0][i + 24]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              mxp[i] = fmaxf(fmaxf(mxp[i], sv[1][i]), fmaxf(sv[1][i + 8], sv[1][i + 16]));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(mxp[i], sv[1][i + 24]);
+            const float hm = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+            const bool up = hm * c2 > m2 + kFwdSlack;
+            if (__any_sync(0xffffffffu, up)) {
+              const float m_new = up ? hm * c2 : m2;
+              const float alpha = ex2(m2 - m_new);   // 0 while m2 is -inf
+              l *= alpha;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) sp[i] *= alpha;
+              if (j > 0) {
+#pragma unroll 1
+                for (int c16 = 0; c16 < 4 * NCH; ++c16) {
+                  if (c16 * 16 < DP) {
+                    float ov[16];
+                    tmem_ld16(tO + c16 * 16, ov);
+                    tmem_wait_ld();
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(ov[i] * alpha);
+                    tmem_st16(tO + c16 * 16, w);
+                  }
+                }
+              }
+              if (h == 1) {
+                tmem_wait_st();
+#pragma unroll 1
+                for (int c16 = 0; c16 < 2; ++c16) {
+                  float pw[16];
+                  tmem_ld16(tS + c16 * 16, pw);
                   tmem_wait_ld();
                   uint32_t w[16];
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(ov[i] * alpha);
-                  tmem_st16(tO + c16 * 16, w);
+                  for (int i = 0; i < 16; ++i) {
+                    const float2 pp = Elt<T>::unpack(__float_as_uint(pw[i]));
+                    w[i] = Elt<T>::pack(pp.x * alpha, pp.y * alpha);
+                  }
+                  tmem_st16(tS + c16 * 16, w);
                 }
               }
+              m2 = m_new;
             }
-            m2 = m_new;
-          }
-          // pass 2: P = exp2(S c2 - m2), row sum; 16-bit P packed in pairs
-          // into TMEM columns [32 h, 32 h + 32) for the keys [64 h, 64 h + 64)
-          // (columns this thread has already read: the write front trails
-          // the read front).
-          float sp[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float sv[2][32];
-            tmem_ld32(tS + h * 64, sv[0]);
-            tmem_ld32(tS + h * 64 + 32, sv[1]);
-            tmem_wait_ld();
 #pragma unroll
             for (int uu = 0; uu < 2; ++uu) {
-              const int cbase = h * 64 + uu * 32;
               uint32_t pk[16];
-              if (cbase + 32 <= nvalid) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  sv[uu][i] = ex2(fmaf(sv[uu][i], c2, -m2));
-                  sp[i & 3] += sv[uu][i];
-                }
-              } else if (cbase < nvalid) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  sv[uu][i] = (cbase + i < nvalid) ? ex2(fmaf(sv[uu][i], c2, -m2)) : 0.f;
-                  sp[i & 3] += sv[uu][i];
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[uu][i] = 0.f;
+              for (int i = 0; i < 32; ++i) {
+                sv[uu][i] = ex2(fmaf(sv[uu][i], c2, -m2));
+                sp[i & 3] += sv[uu][i];
               }
 #pragma unroll
               for (int i = 0; i < 16; ++i) pk[i] = Elt<T>::pack(sv[uu][2 * i], sv[uu][2 * i + 1]);
