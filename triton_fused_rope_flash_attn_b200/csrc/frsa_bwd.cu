@@ -465,13 +465,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         const int kq = valid16(i_), kkeys = valid16(j_);
         for (int kk = 0; kk < kq; ++kk) {
-          const uint32_t aoff = (kk & 3) * 32;
+          // P and dS [key][query] are the A operands, read from TMEM: query
+          // columns [16 kk, 16 kk + 16) sit packed in columns
+          // 64 (kk / 4) + 8 (kk % 4) of the S^T and dP^T regions.
+          const uint32_t pcol = 64 * (kk >> 2) + 8 * (kk & 3);
           const uint32_t acc = (i_ == 0 && kk == 0) ? 0u : 1u;
-          // dV += P dO : A = P [key][query] K-major, B = dO [query][d] MN-major.
-          mma_ss(tDV, sw128_desc(smem_u32(sm.p[kk >> 2]) + aoff, 16, 1024),
+          // dV += P dO : B = dO [query][d] MN-major.
+          mma_ts(tDV, tST + pcol,
                  sw128_desc(smem_u32(sm.dO[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
           // dK^ += dS Q^ : B = Q^ [query][d] MN-major.
-          mma_ss(tDK, sw128_desc(smem_u32(sm.ds[kk >> 2]) + aoff, 16, 1024),
+          mma_ts(tDK, tDPT + pcol,
                  sw128_desc(smem_u32(sm.q[qs][0]) + kk * 2048, kChunkBytes, 1024), idKV, acc);
         }
         // dQ^_j = dS^T K^ : A = dS read query-major (MN-major), B = K^ [key][d]
@@ -805,7 +808,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           // through zero K^ rows, so no per-element masking is needed.
           const uint32_t lbase = smem_u32(&sm.lse2[qs][g * 64]);
           const uint32_t ebase = smem_u32(&sm.delta[qs][g * 64]);
-          const uint32_t pbase = smem_u32(sm.p[g]), dbase = smem_u32(sm.ds[g]);
+          const uint32_t dbase = smem_u32(sm.ds[g]);
           uint32_t pk[2][16], dk[2][16];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
@@ -832,11 +835,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               if (!kAhead) stage_acquire(true);
               if (ts >= 0) FRSA_STAMP(ts + 4);
               if (64 * g < ncol) {
+                tmem_st16(tST + lane_off + g * 64, pk[0]);
+                tmem_st16(tDPT + lane_off + g * 64, dk[0]);
 #pragma unroll
                 for (int g4 = 0; g4 < 4; ++g4) {
                   const uint32_t off = sw128_off(r, g4);
-                  sts_u4(pbase + off, make_uint4(pk[0][4 * g4], pk[0][4 * g4 + 1],
-                                                 pk[0][4 * g4 + 2], pk[0][4 * g4 + 3]));
                   sts_u4(dbase + off, make_uint4(dk[0][4 * g4], dk[0][4 * g4 + 1],
                                                  dk[0][4 * g4 + 2], dk[0][4 * g4 + 3]));
                 }
@@ -859,15 +862,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
           if (64 * g + 32 < ncol) {
+            tmem_st16(tST + lane_off + g * 64 + 16, pk[1]);
+            tmem_st16(tDPT + lane_off + g * 64 + 16, dk[1]);
 #pragma unroll
             for (int g4 = 0; g4 < 4; ++g4) {
               const uint32_t off = sw128_off(r, 4 + g4);
-              sts_u4(pbase + off, make_uint4(pk[1][4 * g4], pk[1][4 * g4 + 1], pk[1][4 * g4 + 2],
-                                             pk[1][4 * g4 + 3]));
               sts_u4(dbase + off, make_uint4(dk[1][4 * g4], dk[1][4 * g4 + 1], dk[1][4 * g4 + 2],
                                              dk[1][4 * g4 + 3]));
             }
           }
+          tmem_wait_st();
           fence_proxy_async_smem();
           tc_fence_before();
           named_bar(1, kComputeThreads);
