@@ -415,9 +415,10 @@ def roofline_of(B, H, N, D, ms, flops, nbytes, peaks):
 
 
 def launches_per_step(N, D):
-    # fwd + bwd; the general backward adds its Delta pre-pass (the counter
-    # clear is a cudaMemsetAsync, not a kernel of this library).
-    return 2 if (N <= 256 and D <= 64) else 3
+    # fwd + bwd; the general backward adds its row pre-pass and the dQ
+    # finalize pass (the counter clear is a cudaMemsetAsync, not a kernel of
+    # this library).
+    return 2 if (N <= 256 and D <= 64) else 4
 
 
 def gpu_arm(args, world, rank, local):

@@ -14,8 +14,11 @@
 //                   P    = exp2(S^T c2 - lse2_q),  dS = P (dP - Delta_q)  (registers)
 //                   dV  += P dO,  dK^ += dS Q^  (TMEM accumulators)
 //                   dQ^_j = dS^T K^          (TMEM, this key tile's share)
-//                 P and dS are written once to shared memory as [key][query]
-//                 tiles; the dQ product reads the same dS tile query-major.
+//                 P and dS are packed into TMEM over the scores (A operands
+//                 of the dV and dK products); dS also goes to shared memory
+//                 as a [key][query] tile, which the dQ product reads
+//                 query-major.
+//   dq_finalize   dQ = R^T (sum of the partial slots, in slot order) per row.
 //
 // dQ is reduced over key tiles in a fixed order, so the result is bitwise
 // reproducible (the reference's dQ kernel is deterministic too: one program
@@ -23,14 +26,12 @@
 // scaled dQ^ share of query tile i into partial slot s = j % S of the
 // workspace (S = nslot; when key tiles share a slot, j >= S first waits for
 // its predecessor j - S in that slot and adds to it, so each slot holds the
-// in-order sum of its key tiles). It then counts itself in on a per-(head,
-// query tile) arrival counter; the CTA that arrives last sums the S slots in
-// slot order, un-rotates with R^T (fa_rope_full .py:974-993) and writes dQ in
-// the I/O type, then discards the slots' L2 lines (they are dead; this saves
-// their write-back to DRAM). No CTA waits for another unless slots are
-// shared, and then only for a unit claimed S units earlier. Units are claimed
-// in order, so a unit waited for is always held by a running CTA; every wait
-// is bounded.
+// in-order sum of its key tiles). After the main kernel, dq_finalize sums
+// each row's S slots in slot order, un-rotates with R^T (fa_rope_full
+// .py:974-993) and writes dQ in the I/O type. No CTA waits for another
+// unless slots are shared, and then only for a unit claimed S units earlier.
+// Units are claimed in order, so a unit waited for is always held by a
+// running CTA; every wait is bounded.
 //
 // Compared with the reference, S and dP are computed once per (key tile,
 // query tile) pair instead of twice, and no separate dQ pass recomputes them.
@@ -100,7 +101,6 @@ struct BwdSmem {
   uint64_t unit_full[kUnitRing], unit_empty[kUnitRing];
   uint64_t stage_full, stage_free;   // result jobs: row warps -> store warps
   int job_type, job_bh, job_j, job_i;
-  int red_flag, red_bh, red_i;       // store warps -> row warps: a query tile to complete
   int unit[kUnitRing];
   uint32_t tmem_base;
   int abort_flag;
@@ -119,7 +119,7 @@ struct BwdParams {
   void* dk;
   void* dv;
   float* dq_part;    // f32 [nslot][BH, N, D] partial dQ^ sums (no initial value needed)
-  int* arrive;       // [BH * nqt] arrival counters, zero at launch
+  int* arrive;       // [BH * nqt] (reserved in the workspace layout; unused)
   int* turns;        // [BH * nqt * nslot] slot turn counters, zero at launch
   int* ticket;       // unit claim counter, zero at launch
   int nslot;         // partial slots S (1 .. nkv)
@@ -128,123 +128,6 @@ struct BwdParams {
   float c2;     // scale * log2(e)
   float scale;
 };
-
-// Complete query tile i of head bh (run by the 256 row threads; rw0 = the
-// warp's first row): every key tile has added its share, so sum the S slots
-// in slot order, un-rotate with R^T (fa_rope_full .py:974-993), store the dQ
-// rows (quad layout: 8 lanes per 128-byte row segment, all slots' loads
-// issued before the sums), then drop the slots' lines from L2 without a
-// write-back.
-template <typename T, int NCH>
-__device__ __forceinline__ void complete_dq_tile(const BwdParams& prm, int bh, int i, int rw0,
-                                              int lane) {
-  constexpr int RW = kRowsPerWarp;
-  const int N = prm.N, D = prm.D, S = prm.nslot;
-  const size_t head_elems = static_cast<size_t>(N) * D;
-  const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
-  __threadfence();
-  const int rq = lane >> 3, gl = lane & 7;
-  const int q0 = i * kTile;
-  T* dq_head = reinterpret_cast<T*>(prm.dq) + static_cast<size_t>(bh) * head_elems;
-  const float* part0 = prm.dq_part + static_cast<size_t>(bh) * head_elems;
-  constexpr int KQ = RW / 4;   // quads of rows per warp
-  if constexpr (NCH == 1) {
-    // The warp's four quads are summed together, one slot per round (8
-    // loads in flight per lane): S L2 round trips per completion.
-    float v[KQ][8];
-    const float4* src[KQ];
-    bool ok[KQ];
-#pragma unroll
-    for (int k = 0; k < KQ; ++k) {
-      const int tk = q0 + rw0 + 4 * k + rq;
-      ok[k] = tk < N && 8 * gl < D;
-      src[k] = reinterpret_cast<const float4*>(part0 + static_cast<size_t>(ok[k] ? tk : 0) * D +
-                                               8 * gl);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
-    }
-#pragma unroll 1
-    for (int sl = 0; sl < S; ++sl) {
-      float4 a[KQ], bq[KQ];
-#pragma unroll
-      for (int k = 0; k < KQ; ++k)
-        if (ok[k]) {
-          a[k] = __ldcg(src[k] + sl * (slot_stride / 4));
-          bq[k] = __ldcg(src[k] + sl * (slot_stride / 4) + 1);
-        }
-#pragma unroll
-      for (int k = 0; k < KQ; ++k)
-        if (ok[k]) {
-          // slot order: v starts at 0, and 0 + x == x
-          v[k][0] += a[k].x; v[k][1] += a[k].y; v[k][2] += a[k].z; v[k][3] += a[k].w;
-          v[k][4] += bq[k].x; v[k][5] += bq[k].y; v[k][6] += bq[k].z; v[k][7] += bq[k].w;
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < KQ; ++k) {
-      const int tk = q0 + rw0 + 4 * k + rq;
-      if (!ok[k]) continue;
-      const int p2 = rope_pos(tk, N, prm.has_cls);
-      if (p2 >= 0) {
-        const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
-        unrotate8(v[k], __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gl),
-                  __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gl));
-      }
-      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gl) = pack8<T>(v[k]);
-    }
-  } else {
-    // One granule at a time, four slots' loads in flight: KQ * NCH *
-    // ceil(S / 4) L2 round trips per completion.
-#pragma unroll 1
-    for (int kh = 0; kh < KQ * NCH; ++kh) {
-      const int k = kh / NCH, h = kh - k * NCH;
-      const int tk = q0 + rw0 + 4 * k + rq;
-      const int gg = gl + 8 * h;
-      if (tk >= N || 8 * gg >= D) continue;
-      const float4* src =
-          reinterpret_cast<const float4*>(part0 + static_cast<size_t>(tk) * D + 8 * gg);
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s0 = 0; s0 < kMaxDqSlots; s0 += 4) {
-        if (s0 >= S) break;
-        float4 a[4], bq[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (s0 + u < S) {
-            a[u] = __ldcg(src + (s0 + u) * (slot_stride / 4));
-            bq[u] = __ldcg(src + (s0 + u) * (slot_stride / 4) + 1);
-          }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (s0 + u < S) {
-            v[0] += a[u].x; v[1] += a[u].y; v[2] += a[u].z; v[3] += a[u].w;
-            v[4] += bq[u].x; v[5] += bq[u].y; v[6] += bq[u].z; v[7] += bq[u].w;
-          }
-      }
-      const int p2 = rope_pos(tk, N, prm.has_cls);
-      if (p2 >= 0) {
-        const size_t t0 = static_cast<size_t>(p2) * (D >> 1);
-        unrotate8(v, __ldg(reinterpret_cast<const float4*>(prm.cosp + t0) + gg),
-                  __ldg(reinterpret_cast<const float4*>(prm.sinp + t0) + gg));
-      }
-      *reinterpret_cast<uint4*>(dq_head + static_cast<size_t>(tk) * D + 8 * gg) = pack8<T>(v);
-    }
-  }
-  named_bar(1, kComputeThreads);
-  // Only lines wholly inside this tile's rows: a line shared with a
-  // neighbouring tile or head may still be live.
-  const int q_rows = min(kTile, N - q0);
-  const int tid = threadIdx.x - 128;
-  for (int sl = 0; sl < S; ++sl) {
-    const uintptr_t lo =
-        reinterpret_cast<uintptr_t>(part0 + sl * slot_stride + static_cast<size_t>(q0) * D);
-    const uintptr_t hi = lo + static_cast<uintptr_t>(q_rows) * D * 4;
-    const uintptr_t l0 = (lo + 127) & ~static_cast<uintptr_t>(127);
-    for (uintptr_t ln = l0 + 128 * static_cast<uintptr_t>(tid); ln + 128 <= hi;
-         ln += 128 * kComputeThreads)
-      discard_l2_line(reinterpret_cast<const void*>(ln));
-  }
-}
 
 template <typename T, int NCH>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -375,15 +258,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
     const int S = prm.nslot;
     const bool issuer = threadIdx.x == 64;
-    const size_t head_elems = static_cast<size_t>(N) * D;
-    const size_t slot_stride = static_cast<size_t>(prm.BH) * head_elems;
     for (int m = 0;; ++m) {
       mbar_wait(&sm.stage_full, m & 1, abort_flag);
       const int type = *abort_flag ? 0 : *reinterpret_cast<volatile int*>(&sm.job_type);
       const int bh = sm.job_bh, j = sm.job_j, i = sm.job_i;
       if (type == 0) break;    // no more jobs
       if (issuer) {
-        bool last = false;
         if (type == 1) {
           // dV chunk c at stage chunk c, dK chunk c at stage chunk NCH + c.
           for (int c = 0; c < NCH; ++c) {
@@ -395,7 +275,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           tma_store_commit();
           tma_store_wait_read();
-          sm.red_flag = 0;
           mbar_arrive(&sm.stage_free);
         } else {
           const int slot = j % S, gen = j / S;
@@ -412,12 +291,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           __threadfence();
           if (j + S < prm.nkv) st_release_gpu(prm.turns + (static_cast<size_t>(bh) * nqt + i) * S +
                                                   slot, gen + 1);
-          last = atomicAdd(prm.arrive + static_cast<size_t>(bh) * nqt + i, 1) == prm.nkv - 1;
-          // The key tile arriving last completes the query tile: the row
-          // warps pick this up when they next acquire the stage.
-          sm.red_flag = last ? 1 : 0;
-          sm.red_bh = bh;
-          sm.red_i = i;
           mbar_arrive(&sm.stage_free);
         }
       }
@@ -635,24 +508,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
     const uint32_t stb = smem_u32(stage);
 #ifdef FRSA_TRACE
-    unsigned trace_flags = 0;   // events of the current iteration (bit 0: a dQ tile completed)
+    unsigned trace_flags = 0;   // events of the current iteration
 #endif
     int jobs = 0;   // jobs posted so far
     int acquired = 0;   // jobs whose stage release has been taken
-    // Wait until the store warps are done with the stage (the last posted
-    // job), and complete the query tile that job finished, if any.
-    // (after_dq: the last posted job may have been a dQ share; a dV/dK job
-    // never completes a query tile.)
-    auto stage_acquire = [&](bool after_dq) {
+    // Wait until the store warp is done with the stage (the last posted job).
+    auto stage_acquire = [&]() {
       if (jobs == acquired) return;
       mbar_wait(&sm.stage_free, (jobs - 1) & 1, abort_flag);
       acquired = jobs;
-      if (after_dq && *reinterpret_cast<volatile int*>(&sm.red_flag) && !*abort_flag) {
-        complete_dq_tile<T, NCH>(prm, sm.red_bh, sm.red_i, rw0, lane);
-#ifdef FRSA_TRACE
-        trace_flags |= 1u;
-#endif
-      }
     };
     auto post = [&](int type, int bh_, int j_, int i_) {
       fence_proxy_async_smem();
@@ -691,9 +555,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (leader) mbar_arrive(&sm.dq_free);
       }
       if (trace_ts >= 0) FRSA_STAMP(trace_ts + 6);
-      // (without kAhead the previous dQ job was already taken, and its query
-      // tile completed, before this iteration's P/dS were stored)
-      stage_acquire(kAhead || flush);
+      // (without kAhead the previous dQ job was already taken before this
+      // iteration's dS was stored)
+      stage_acquire();
       if (flush) return;
       if (unit_end) {
         const int kv0 = j_ * kTile;
@@ -729,7 +593,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         post(1, bh_, j_, i_);
         if (leader) mbar_arrive(&sm.acc_free);
-        stage_acquire(false);
+        stage_acquire();
       }
 #pragma unroll
       for (int b = 0; b < kBlk / 2; ++b) {
@@ -832,7 +696,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 mbar_wait(&sm.mm_done, (t - 1) & 1, abort_flag);
                 tc_fence_after();
               }
-              if (!kAhead) stage_acquire(true);
+              if (!kAhead) stage_acquire();
               if (ts >= 0) FRSA_STAMP(ts + 4);
               if (64 * g < ncol) {
                 tmem_st16(tST + lane_off + g * 64, pk[0]);
@@ -920,7 +784,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ++t;
       }
     }
-    if (u < 0) stage_acquire(false);   // (no work: nothing was posted)
+    if (u < 0) stage_acquire();   // (no work: nothing was posted)
     post(0, 0, 0, 0);   // no more jobs
     FRSA_STAMP(57);
 #ifdef FRSA_TRACE
@@ -1032,6 +896,55 @@ __global__ void prep_rows_kernel(const PrepRows p) {
     acc += __shfl_xor_sync(0xffffffffu, acc, 4);
     if (gl == 0 && valid) p.delta[row] = acc;
   }
+}
+
+// dQ from the partial slots, after bwd_kernel: every key tile has added its
+// scaled dQ^ share into its slot, so each row's dQ^ is the sum of the S
+// slots in slot order, un-rotated with R^T (fa_rope_full .py:974-993) and
+// stored in the I/O type. One thread per 8-element granule of a row, all S
+// slots' loads in flight at once; the grid streams the slots from memory.
+// Run as its own launch so that the sums do not sit on the main kernel's
+// critical path (they used to be done inside it by the CTA whose key tile
+// arrived last, one L2 round trip per slot).
+struct DqFinal {
+  const float* part;        // [nslot][rows, D] f32
+  void* dq;                 // [rows, D] I/O type
+  const float* cosp;
+  const float* sinp;
+  long long rows, slot_stride;
+  int nslot, N, D, has_cls;
+};
+
+template <typename T>
+__global__ void dq_finalize_kernel(const DqFinal p) {
+  const int G = p.D >> 3;   // granules of a row
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long row = idx / G;
+  if (row >= p.rows) return;
+  const int gg = static_cast<int>(idx - row * G);
+  const float4* src = reinterpret_cast<const float4*>(p.part + row * p.D) + 2 * gg;
+  float4 a[kMaxDqSlots], b[kMaxDqSlots];
+#pragma unroll
+  for (int s = 0; s < kMaxDqSlots; ++s)
+    if (s < p.nslot) {
+      a[s] = __ldcs(src + s * (p.slot_stride / 4));
+      b[s] = __ldcs(src + s * (p.slot_stride / 4) + 1);
+    }
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < kMaxDqSlots; ++s)
+    if (s < p.nslot) {   // slot order: v starts at 0, and 0 + x == x
+      v[0] += a[s].x; v[1] += a[s].y; v[2] += a[s].z; v[3] += a[s].w;
+      v[4] += b[s].x; v[5] += b[s].y; v[6] += b[s].z; v[7] += b[s].w;
+    }
+  const int n = static_cast<int>(row % p.N);
+  const int pos = rope_pos(n, p.N, p.has_cls);
+  if (pos >= 0) {
+    const size_t t0 = static_cast<size_t>(pos) * (p.D >> 1);
+    unrotate8(v, __ldg(reinterpret_cast<const float4*>(p.cosp + t0) + gg),
+              __ldg(reinterpret_cast<const float4*>(p.sinp + t0) + gg));
+  }
+  reinterpret_cast<uint4*>(static_cast<T*>(p.dq) + row * p.D)[gg] = pack8<T>(v);
 }
 
 }  // namespace
@@ -1169,15 +1082,34 @@ cudaError_t launch_bwd_ordered(const LaunchShape& s, const CUtensorMap& tm_q,
     p.delta_out = nullptr;   // delta_buf is the caller's delta when one was given
   }
   if (s.bf16)
-    return (s.D > 64)
-               ? launch_bwd_main<__nv_bfloat16, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
-                                                   tm_part, p, stream)
-               : launch_bwd_main<__nv_bfloat16, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
-                                                   tm_part, p, stream);
-  return (s.D > 64) ? launch_bwd_main<__half, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
-                                                 tm_part, p, stream)
-                    : launch_bwd_main<__half, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
-                                                 tm_part, p, stream);
+    e = (s.D > 64) ? launch_bwd_main<__nv_bfloat16, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk,
+                                                       tm_dv, tm_part, p, stream)
+                   : launch_bwd_main<__nv_bfloat16, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk,
+                                                       tm_dv, tm_part, p, stream);
+  else
+    e = (s.D > 64) ? launch_bwd_main<__half, 2>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                tm_part, p, stream)
+                   : launch_bwd_main<__half, 1>(s, tm_q, tm_k, tm_v, tm_do, tm_o, tm_dk, tm_dv,
+                                                tm_part, p, stream);
+  if (e != cudaSuccess) return e;
+  DqFinal f;
+  f.part = dq_part;
+  f.dq = dq;
+  f.cosp = cosp;
+  f.sinp = sinp;
+  f.rows = rows;
+  f.slot_stride = rows * s.D;
+  f.nslot = nslot;
+  f.N = s.N;
+  f.D = s.D;
+  f.has_cls = s.has_cls;
+  const long long threads_f = rows * (s.D / 8);
+  const unsigned blocks_f = static_cast<unsigned>((threads_f + 255) / 256);
+  if (s.bf16)
+    dq_finalize_kernel<__nv_bfloat16><<<blocks_f, 256, 0, stream>>>(f);
+  else
+    dq_finalize_kernel<__half><<<blocks_f, 256, 0, stream>>>(f);
+  return cudaGetLastError();
 }
 
 }  // namespace frsa
