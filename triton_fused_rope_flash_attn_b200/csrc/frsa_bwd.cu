@@ -287,10 +287,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             else tma_store_3d(&tm_part, stage + h * kChunkBytes, 32 * h, i * kTile, z);
           }
           tma_store_commit();
-          tma_store_wait_all();   // the share is in L2 (and the stage read)
-          __threadfence();
-          if (j + S < prm.nkv) st_release_gpu(prm.turns + (static_cast<size_t>(bh) * nqt + i) * S +
-                                                  slot, gen + 1);
+          if (j + S < prm.nkv) {
+            // A later key tile adds to this slot: the share must be in L2
+            // before its turn is released.
+            tma_store_wait_all();
+            __threadfence();
+            st_release_gpu(prm.turns + (static_cast<size_t>(bh) * nqt + i) * S + slot, gen + 1);
+          } else {
+            tma_store_wait_read();   // only the stage must be free (the kernel's end waits for the writes)
+          }
           mbar_arrive(&sm.stage_free);
         }
       }
