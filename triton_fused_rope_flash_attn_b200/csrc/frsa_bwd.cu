@@ -87,12 +87,11 @@ struct BwdSmem {
   uint8_t v[KVS][NCH][kChunkBytes];
   uint8_t q[QS][NCH][kChunkBytes];
   uint8_t dO[QS][NCH][kChunkBytes];
-  uint8_t p[2][kChunkBytes];   // P  [128 key][128 query], two 64-column chunks
-  uint8_t ds[2][kChunkBytes];  // dS [128 key][128 query]
+  uint8_t ds[2][kChunkBytes];  // dS [128 key][128 query], two 64-column chunks
   // Store staging for one CTA-wide result tile (D <= 64: the dV and dK^
-  // tiles, then the f32 dQ^ share); with one query stage the P/dS tiles,
-  // which are idle while results drain, serve instead.
-  uint8_t stage[(NCH == 1) ? 2 : 1][kChunkBytes];
+  // tiles, then the f32 dQ^ share). With one query stage the dS tile, idle
+  // while results drain, and this area form one four-chunk stage.
+  uint8_t stage[2][kChunkBytes];
   alignas(16) float lse2[QS][kTile];   // lse * log2(e) of the query tile (read as float4)
   alignas(16) float delta[QS][kTile];
   uint64_t kv_full[KVS], kv_empty[KVS];
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // it arrived last, the row warps are told (with the stage's release) to
     // complete that query tile's dQ. Nothing here waits on the row warps
     // beyond the job hand-off.
-    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
+    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.ds[0][0];
     const int S = prm.nslot;
     const bool issuer = threadIdx.x == 64;
     for (int m = 0;; ++m) {
@@ -510,7 +509,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     //   job 2: a dQ^ share * scale, f32 tiles [128 query][32] (128-byte
     //          swizzle), 32-column block h at stage chunk h;
     //   job 0: no more jobs.
-    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.p[0][0];
+    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.ds[0][0];
     const uint32_t stb = smem_u32(stage);
 #ifdef FRSA_TRACE
     unsigned trace_flags = 0;   // events of the current iteration
