@@ -88,18 +88,23 @@ struct BwdSmem {
   uint8_t q[QS][NCH][kChunkBytes];
   uint8_t dO[QS][NCH][kChunkBytes];
   uint8_t ds[2][kChunkBytes];  // dS [128 key][128 query], two 64-column chunks
-  // Store staging for one CTA-wide result tile (D <= 64: the dV and dK^
-  // tiles, then the f32 dQ^ share). With one query stage the dS tile, idle
-  // while results drain, and this area form one four-chunk stage.
-  uint8_t stage[2][kChunkBytes];
+  // Store staging. D <= 64: two areas of two chunks, one for the f32 dQ^
+  // shares and one for the dV and dK^ tiles, each with its own store thread,
+  // so a unit's dV/dK store and its last dQ^ share are in flight together.
+  // With one query stage the dS tile, idle while results drain, and this
+  // area form one four-chunk stage for all results.
+  static constexpr int NSTAGE = (NCH == 1) ? 4 : 2;
+  uint8_t stage[NSTAGE][kChunkBytes];
   alignas(16) float lse2[QS][kTile];   // lse * log2(e) of the query tile (read as float4)
   alignas(16) float delta[QS][kTile];
   uint64_t kv_full[KVS], kv_empty[KVS];
   uint64_t q_full[QS], q_empty[QS];
   uint64_t kq_ready, st_full, st_free, ds_full, mm_done, dq_free, acc_free;
   uint64_t unit_full[kUnitRing], unit_empty[kUnitRing];
-  uint64_t stage_full, stage_free;   // result jobs: row warps -> store warps
-  int job_type, job_bh, job_j, job_i;
+  // Result jobs, row warps -> store threads, on channel 0 (dQ^ shares, and
+  // everything when there is one stage area) and channel 1 (dV/dK).
+  uint64_t stage_full[2], stage_free[2];
+  int job_type[2], job_bh[2], job_j[2], job_i[2];
   int unit[kUnitRing];
   uint32_t tmem_base;
   int abort_flag;
@@ -169,8 +174,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&sm.st_free, 1);
     mbar_init(&sm.dq_free, 1);
     mbar_init(&sm.acc_free, 1);
-    mbar_init(&sm.stage_full, 1);
-    mbar_init(&sm.stage_free, 1);
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&sm.stage_full[c], 1);
+      mbar_init(&sm.stage_free[c], 1);
+    }
     for (int s = 0; s < kUnitRing; ++s) {
       mbar_init(&sm.unit_full[s], 1);
       mbar_init(&sm.unit_empty[s], 1 + kComputeThreads);
@@ -188,6 +195,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + DP;
   const uint32_t tDQ = (256 + 3 * DP <= 512) ? tmem + 256 + 2 * DP : tDPT;
   constexpr bool kAhead = (QS == 2);   // S^T/dP^T of t + 1 ahead of t's gradient products
+  constexpr bool kSplit = Sm::NSTAGE == 4;   // separate stage areas for dQ^ and dV/dK
   // Number of 16-token steps of tile t that hold tokens (8 for a full tile):
   // products skip the steps of a last tile that are only padding.
   auto valid16 = [&](int t) -> int { return min(8, (N - t * kTile + 15) >> 4); };
@@ -244,37 +252,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp >= 2) {
-    // ------------------------------------------------------------ store warps
-    // Warps 2 and 3 take finished result tiles from the stage (jobs posted by
-    // the row warps) and write them with TMA stores issued by lane 0 of warp
-    // 2: dV/dK tiles, and dQ^ shares into their partial slot (a plain store
-    // for the first key tile of the slot, else an L2 reduce-add after that
-    // slot's turn). Once a share is in L2 the slot's next turn is released and
-    // the key tile counted in on the (head, query tile) arrival counter; when
-    // it arrived last, the row warps are told (with the stage's release) to
-    // complete that query tile's dQ. Nothing here waits on the row warps
-    // beyond the job hand-off.
-    uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.ds[0][0];
-    const int S = prm.nslot;
-    const bool issuer = threadIdx.x == 64;
-    for (int m = 0;; ++m) {
-      mbar_wait(&sm.stage_full, m & 1, abort_flag);
-      const int type = *abort_flag ? 0 : *reinterpret_cast<volatile int*>(&sm.job_type);
-      const int bh = sm.job_bh, j = sm.job_j, i = sm.job_i;
-      if (type == 0) break;    // no more jobs
-      if (issuer) {
+    // ------------------------------------------------------------ store threads
+    // Lane 0 of warp 2 (channel 0) and, with two stage areas, lane 0 of warp
+    // 3 (channel 1) take finished result tiles from their stage area (jobs
+    // posted by the row warps) and write them with TMA stores: dV/dK tiles,
+    // and dQ^ shares into their partial slot (a plain store for the first key
+    // tile of the slot, else an L2 reduce-add after that slot's turn; once a
+    // share is in L2 the slot's next turn is released). Nothing here waits on
+    // the row warps beyond the job hand-off.
+    const int ch = warp - 2;
+    if (lane == 0 && (ch == 0 || kSplit)) {
+      uint8_t* stage = kAhead ? &sm.stage[0][0] : &sm.ds[0][0];
+      uint8_t* kv_area = stage + (kSplit ? 2 * kChunkBytes : 0);
+      const int S = prm.nslot;
+      for (int m = 0;; ++m) {
+        mbar_wait(&sm.stage_full[ch], m & 1, abort_flag);
+        const int type = *abort_flag ? 0 : *reinterpret_cast<volatile int*>(&sm.job_type[ch]);
+        const int bh = sm.job_bh[ch], j = sm.job_j[ch], i = sm.job_i[ch];
+        if (type == 0) break;    // no more jobs
         if (type == 1) {
-          // dV chunk c at stage chunk c, dK chunk c at stage chunk NCH + c.
+          // dV chunk c at area chunk c, dK chunk c at area chunk NCH + c.
           for (int c = 0; c < NCH; ++c) {
             if (c * 64 < D) {
-              tma_store_bh(&tm_dv, stage + c * kChunkBytes, c * kChunkCols, j * kTile, bh, prm.H);
-              tma_store_bh(&tm_dk, stage + (NCH + c) * kChunkBytes, c * kChunkCols, j * kTile, bh,
-                           prm.H);
+              tma_store_bh(&tm_dv, kv_area + c * kChunkBytes, c * kChunkCols, j * kTile, bh, prm.H);
+              tma_store_bh(&tm_dk, kv_area + (NCH + c) * kChunkBytes, c * kChunkCols, j * kTile,
+                           bh, prm.H);
             }
           }
           tma_store_commit();
           tma_store_wait_read();
-          mbar_arrive(&sm.stage_free);
+          mbar_arrive(&sm.stage_free[ch]);
         } else {
           const int slot = j % S, gen = j / S;
           if (gen > 0)
@@ -295,11 +302,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           } else {
             tma_store_wait_read();   // only the stage must be free (the kernel's end waits for the writes)
           }
-          mbar_arrive(&sm.stage_free);
+          mbar_arrive(&sm.stage_free[ch]);
         }
       }
+      tma_store_wait_all();
     }
-    if (issuer) tma_store_wait_all();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -514,25 +521,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #ifdef FRSA_TRACE
     unsigned trace_flags = 0;   // events of the current iteration
 #endif
-    int jobs = 0;   // jobs posted so far
-    int acquired = 0;   // jobs whose stage release has been taken
-    // Wait until the store warp is done with the stage (the last posted job).
-    auto stage_acquire = [&]() {
-      if (jobs == acquired) return;
-      mbar_wait(&sm.stage_free, (jobs - 1) & 1, abort_flag);
-      acquired = jobs;
+    const uint32_t stb_kv = stb + (kSplit ? 2 * kChunkBytes : 0);   // dV/dK area
+    constexpr int kKvCh = kSplit ? 1 : 0;                             // dV/dK channel
+    int jobs[2] = {0, 0};       // jobs posted so far, per channel
+    int acquired[2] = {0, 0};   // jobs whose stage release has been taken
+    // Wait until the store thread of channel c is done with its area (the
+    // last job posted on c).
+    auto stage_acquire = [&](int c) {
+      if (jobs[c] == acquired[c]) return;
+      mbar_wait(&sm.stage_free[c], (jobs[c] - 1) & 1, abort_flag);
+      acquired[c] = jobs[c];
     };
-    auto post = [&](int type, int bh_, int j_, int i_) {
+    auto post = [&](int c, int type, int bh_, int j_, int i_) {
       fence_proxy_async_smem();
       named_bar(1, kComputeThreads);
       if (leader) {
-        sm.job_type = type;
-        sm.job_bh = bh_;
-        sm.job_j = j_;
-        sm.job_i = i_;
-        mbar_arrive(&sm.stage_full);
+        sm.job_type[c] = type;
+        sm.job_bh[c] = bh_;
+        sm.job_j[c] = j_;
+        sm.job_i[c] = i_;
+        mbar_arrive(&sm.stage_full[c]);
       }
-      ++jobs;
+      ++jobs[c];
     };
 
     // Results of a finished iteration (its products done, mm_done waited):
@@ -561,9 +571,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (trace_ts >= 0) FRSA_STAMP(trace_ts + 6);
       // (without kAhead the previous dQ job was already taken before this
       // iteration's dS was stored)
-      stage_acquire();
-      if (flush) return;
+      if (flush) {
+        stage_acquire(0);
+        stage_acquire(kKvCh);
+        return;
+      }
       if (unit_end) {
+        stage_acquire(kKvCh);
         const int kv0 = j_ * kTile;
         const int pos = rope_pos(kv0 + r, N, prm.has_cls);
 #pragma unroll 1
@@ -589,16 +603,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                           __ldg(reinterpret_cast<const float4*>(prm.sinp + t0)));
               }
               const uint32_t gr = static_cast<uint32_t>((c16 & 3) * 2 + h8);
-              sts_u4(stb + c * kChunkBytes + sw128_off(r, gr), pack8<T>(a));
-              sts_u4(stb + (NCH + c) * kChunkBytes + sw128_off(r, gr), pack8<T>(bk));
+              sts_u4(stb_kv + c * kChunkBytes + sw128_off(r, gr), pack8<T>(a));
+              sts_u4(stb_kv + (NCH + c) * kChunkBytes + sw128_off(r, gr), pack8<T>(bk));
             }
           }
         }
         tc_fence_before();
-        post(1, bh_, j_, i_);
+        post(kKvCh, 1, bh_, j_, i_);
         if (leader) mbar_arrive(&sm.acc_free);
-        stage_acquire();
       }
+      stage_acquire(0);
 #pragma unroll
       for (int b = 0; b < kBlk / 2; ++b) {
         const int c16 = g + 2 * b;
@@ -619,7 +633,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       if (!kAhead) tc_fence_before();
-      post(2, bh_, j_, i_);
+      post(0, 2, bh_, j_, i_);
       if (!kAhead && leader) mbar_arrive(&sm.dq_free);
     };
 
@@ -700,7 +714,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 mbar_wait(&sm.mm_done, (t - 1) & 1, abort_flag);
                 tc_fence_after();
               }
-              if (!kAhead) stage_acquire();
+              if (!kAhead) stage_acquire(0);
               if (ts >= 0) FRSA_STAMP(ts + 4);
               if (64 * g < ncol) {
                 tmem_st16(tST + lane_off + g * 64, pk[0]);
@@ -788,8 +802,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ++t;
       }
     }
-    if (u < 0) stage_acquire();   // (no work: nothing was posted)
-    post(0, 0, 0, 0);   // no more jobs
+    // no more jobs (stage_acquire: with no work nothing was posted)
+    if (u < 0) stage_acquire(0);
+    post(0, 0, 0, 0, 0);
+    if (kSplit) post(1, 0, 0, 0, 0);
     FRSA_STAMP(57);
 #ifdef FRSA_TRACE
     if (threadIdx.x == FRSA_STAMP_TID && blockIdx.x < 2048) g_trace[blockIdx.x * 64 + 58] = t + 1;
