@@ -121,6 +121,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int nkv = prm.nkv;
   const int DP = (D + 15) & ~15;   // MMA N for P V
   const int ksteps = DP >> 4;      // MMA K steps over the head dim
+  // D <= 64 and at least two key tiles: O alternates between two 64-column
+  // TMEM buffers per unit, and a unit's O epilogue is deferred into the next
+  // unit (after that unit's first P is published, while its second scores
+  // are computed), so the softmax warps neither wait for the unit's last P V
+  // nor stall the next unit on the O read-out.
+  const bool two_o = NCH == 1 && nkv >= 2;
   volatile int* abort_flag = &sm.abort_flag;
   int ubeg, uend;
   fwd_range(prm, ubeg, uend);
@@ -213,15 +219,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // O_g (+)= P_g V : A = P [q][kv] from TMEM (packed 16-bit pairs over
       // the scores: keys [16 ks, 16 ks + 16) in columns [8 ks, 8 ks + 8)),
       // B = V [kv][d] MN-major. O accumulates over a unit's key tiles.
-      auto issue_pv = [&](int g, int s, bool acc) {
+      auto issue_pv = [&](int g, int s, bool acc, uint32_t ocol) {
         const uint32_t tS = tmem + 256 * g;
-        const uint32_t tO = tS + 128;
+        const uint32_t tO = tS + ocol;
         for (int ks = 0; ks < kTile / 16; ++ks)
           mma_ts(tO, tS + 8 * ks, sw128_desc(smem_u32(sm.v[s][0]) + ks * 2048, kChunkBytes, 1024),
                  idO, acc || ks > 0);
       };
       int qf[2] = {0, 0};   // query-tile fill of the current unit, per warpgroup
       int tg[2] = {0, 0};   // key tiles processed, per warpgroup
+      int ug[2] = {0, 0};   // units finished, per warpgroup (selects the O buffer)
       int t = 0;            // running K/V tile
       int u = ubeg;
       FwdUnit x = fwd_unit(prm, u);
@@ -262,10 +269,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               v_waited = true;
             }
             tc_fence_after();
-            issue_pv(g, s, j > 0);
+            issue_pv(g, s, j > 0, 128 + (two_o ? 64 * (ug[g] & 1) : 0));
             ++tg[g];
             if (!more) {
               mma_commit(&sm.o_full[g]);
+              ++ug[g];
             } else {
               wait_k();
               tc_fence_after();
@@ -347,7 +355,54 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tS = tmem + 256 * g + lane_off;
     const uint32_t tO = tmem + 256 * g + 128 + lane_off;
     int tg0 = 0;   // key tiles this warpgroup processed in earlier units
-    int uo = 0;    // units this warpgroup finished (o_full phase)
+    int uo = 0;    // unit epilogues this warpgroup has waited for (o_full phase)
+    int uc = 0;    // units this warpgroup has started (O buffer with two_o)
+    // O / l of a finished unit, read from O buffer `tob` once its last P V
+    // has completed, stored from registers (thread = query row; tcgen05.ld
+    // is warp-collective, so the loads run in every lane of an active warp
+    // and the stores only for rows that hold tokens).
+    auto o_epilogue = [&](int bh_, int qrow_, float l_, bool active_, uint32_t tob) {
+      mbar_wait(&sm.o_full[g], uo & 1, abort_flag);
+      tc_fence_after();
+      ++uo;
+      if (active_) {
+        const float inv_l = 1.f / l_;
+        uint4* orow = reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.o) +
+                                               (static_cast<size_t>(bh_) * N + qrow_) * D);
+#pragma unroll 1
+        for (int c16 = 0; c16 < 8; ++c16) {
+          if (c16 * 16 < DP) {
+            float v[16];
+            tmem_ld16(tob + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] *= inv_l;
+            uint4 w0, w1;
+            w0.x = Elt<T>::pack(v[0], v[1]);
+            w0.y = Elt<T>::pack(v[2], v[3]);
+            w0.z = Elt<T>::pack(v[4], v[5]);
+            w0.w = Elt<T>::pack(v[6], v[7]);
+            w1.x = Elt<T>::pack(v[8], v[9]);
+            w1.y = Elt<T>::pack(v[10], v[11]);
+            w1.z = Elt<T>::pack(v[12], v[13]);
+            w1.w = Elt<T>::pack(v[14], v[15]);
+            if (qrow_ < N) {
+              orow[2 * c16] = w0;
+              if (c16 * 16 + 8 < D) orow[2 * c16 + 1] = w1;
+            }
+          }
+        }
+      }
+      // The O columns have been read: the P V that next overwrites them
+      // follows this group's next p_full arrival.
+      tc_fence_before();
+    };
+    // The deferred epilogue (two_o): unit, row, l, activity and O buffer.
+    bool pend = false;
+    int pend_bh = 0, pend_row = 0;
+    float pend_l = 0.f;
+    bool pend_active = false;
+    uint32_t pend_tob = 0;
 #ifdef FRSA_TRACE
     int tr_i = 0;
 #define FWD_TR(ev, jj)                                                                   \
@@ -371,6 +426,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int bh = x.bh;
       const int q0 = (2 * x.pr + g) * kTile;
       const int qrow = q0 + r;
+      const uint32_t tOc = tO + (two_o ? 64u * static_cast<uint32_t>(uc & 1) : 0u);   // this unit's O
+      ++uc;
       float m2 = -INFINITY, l = 0.f;
       // A warp whose 32 query rows are all padding skips the softmax math: its
       // P rows only ever reach O rows that are not stored.
@@ -445,12 +502,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 for (int c16 = 0; c16 < 4 * NCH; ++c16) {
                   if (c16 * 16 < DP) {
                     float ov[16];
-                    tmem_ld16(tO + c16 * 16, ov);
+                    tmem_ld16(tOc + c16 * 16, ov);
                     tmem_wait_ld();
                     uint32_t w[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(ov[i] * alpha);
-                    tmem_st16(tO + c16 * 16, w);
+                    tmem_st16(tOc + c16 * 16, w);
                   }
                 }
               }
@@ -492,53 +549,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         named_bar(2 + g, 128);
         if (leader) mbar_arrive(&sm.p_full[g]);
         FWD_TR(2, j);
-      }
-
-      // epilogue: lse = (m + log2 l) ln 2 and O / l, read from TMEM once the
-      // unit's last P V has completed and stored from registers (thread =
-      // query row). The next unit's scores are already in flight meanwhile.
-      if (qrow < N)
-        prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
-      mbar_wait(&sm.o_full[g], uo & 1, abort_flag);
-      tc_fence_after();
-      FWD_TR(3, 0);
-      ++uo;
-      tg0 += nkv;
-      // (tcgen05.ld is warp-collective: the loads run in every lane of an
-      // active warp, the stores only for rows that hold tokens)
-      if (warp_active) {
-        const float inv_l = 1.f / l;
-        uint4* orow = reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.o) +
-                                               (static_cast<size_t>(bh) * N + qrow) * D);
-#pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {
-          if (c16 * 16 < DP) {
-            float v[16];
-            tmem_ld16(tO + c16 * 16, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] *= inv_l;
-            uint4 w0, w1;
-            w0.x = Elt<T>::pack(v[0], v[1]);
-            w0.y = Elt<T>::pack(v[2], v[3]);
-            w0.z = Elt<T>::pack(v[4], v[5]);
-            w0.w = Elt<T>::pack(v[6], v[7]);
-            w1.x = Elt<T>::pack(v[8], v[9]);
-            w1.y = Elt<T>::pack(v[10], v[11]);
-            w1.z = Elt<T>::pack(v[12], v[13]);
-            w1.w = Elt<T>::pack(v[14], v[15]);
-            if (qrow < N) {
-              orow[2 * c16] = w0;
-              if (c16 * 16 + 8 < D) orow[2 * c16 + 1] = w1;
-            }
-          }
+        if (pend && j == 0) {   // the previous unit's O, while this unit's next scores run
+          o_epilogue(pend_bh, pend_row, pend_l, pend_active, pend_tob);
+          pend = false;
         }
       }
-      // The O columns have been read: the next unit's first P V may
-      // overwrite them (it follows this group's next p_full arrival).
-      tc_fence_before();
+
+      // epilogue: lse = (m + log2 l) ln 2 now; O / l once the unit's last P V
+      // has completed (deferred into the next unit with two_o).
+      if (qrow < N)
+        prm.lse[static_cast<size_t>(bh) * N + qrow] = (m2 + lg2(l)) * 0.69314718055994531f;
+      tg0 += nkv;
+      if (two_o) {
+        pend = true;
+        pend_bh = bh;
+        pend_row = qrow;
+        pend_l = l;
+        pend_active = warp_active;
+        pend_tob = tOc;
+      } else {
+        o_epilogue(bh, qrow, l, warp_active, tOc);
+      }
       FWD_TR(4, 0);
     }
+    if (pend) o_epilogue(pend_bh, pend_row, pend_l, pend_active, pend_tob);
   }
 
   tc_fence_before();
