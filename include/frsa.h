@@ -188,6 +188,28 @@ typedef struct frsa_qkv_args {
 
 int frsa_qkv_rope(const frsa_qkv_args* args, void* stream);
 
+/* Backward of frsa_qkv_rope's epilogue: from the gradients of its outputs
+ * dq, dk, dv ([B, H, N, D] each, `dtype`, contiguous; dq and dk with respect
+ * to the rotated q and k), writes dqkv [B*N, 3C] (`dtype`), the gradient of
+ * the projection output x w^T + b: R^T applied to the q and k parts in f32,
+ * one rounding, heads merged back into channels. Then dx = dqkv w,
+ * dw = dqkv^T x and db = the column sums of dqkv. Same shape rules as
+ * frsa_qkv_rope (C % 128 == 0, D % 32 == 0). No counterpart in the reference
+ * (see frsa_qkv_rope). */
+typedef struct frsa_qkv_bwd_args {
+  const void* dq;
+  const void* dk;
+  const void* dv;
+  const float* cosp;
+  const float* sinp;
+  void* dqkv;
+  int64_t B, N, C, H, n_pos;
+  int32_t has_cls;
+  int32_t dtype;      /* enum frsa_dtype: BF16 or F16 */
+} frsa_qkv_bwd_args;
+
+int frsa_qkv_rope_bwd(const frsa_qkv_bwd_args* args, void* stream);
+
 /* FRSA_ABI_VERSION of the loaded library. */
 int frsa_abi_version(void);
 

@@ -76,3 +76,40 @@ def test_fused_qkv_rope_block_matches_unfused(dim, heads, side, has_cls):
                      blk.qkv.bias.grad.float()))
     for a, b in zip(*outs):
         assert float((a - b).abs().max() / b.abs().max()) < 2e-2
+
+
+@pytest.mark.parametrize("B,C,H,side,has_cls,dtype", [(2, 768, 12, 14, True, torch.bfloat16),
+                                                      (1, 384, 6, 7, False, torch.float16)])
+def test_qkv_rope_bwd_kernel_matches_torch(B, C, H, side, has_cls, dtype):
+    """frsa_qkv_rope_bwd through the C ABI against its definition in fp32 torch:
+    dqkv[b*N + n] = concat over q, k, v of the head-merged gradients, with R^T
+    (the reference's pair rotation transposed) on the q and k parts."""
+    from triton_fused_rope_flash_attn_b200 import CosSinTable, _lib
+    N = side * side + (1 if has_cls else 0)
+    D = C // H
+    cs = CosSinTable(100.0, side, D, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    dq, dk, dv = (torch.randn(B, H, N, D, device="cuda", generator=g).to(dtype) for _ in range(3))
+    dqkv = torch.empty(B * N, 3 * C, device="cuda", dtype=dtype)
+    a = _lib.FrsaQkvBwdArgs()
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    a.cosp, a.sinp, a.dqkv = cs.COSP.data_ptr(), cs.SINP.data_ptr(), dqkv.data_ptr()
+    a.B, a.N, a.C, a.H, a.n_pos = B, N, C, H, cs.COSP.shape[0]
+    a.has_cls, a.dtype = int(has_cls), (_lib.FRSA_DTYPE_BF16 if dtype == torch.bfloat16
+                                        else _lib.FRSA_DTYPE_F16)
+    assert _lib.load().frsa_qkv_rope_bwd(a, None) == 0
+    torch.cuda.synchronize()
+    off = 1 if has_cls else 0
+    c = torch.ones(N, D // 2, device="cuda")
+    s = torch.zeros(N, D // 2, device="cuda")
+    c[off:], s[off:] = cs.COSP[: N - off], cs.SINP[: N - off]
+    parts = []
+    for t, rot in ((dq, True), (dk, True), (dv, False)):
+        t = t.float()
+        if rot:
+            e, o = t[..., 0::2], t[..., 1::2]
+            t = torch.stack((e * c + o * s, o * c - e * s), dim=-1).flatten(-2)
+        parts.append(t.transpose(1, 2).reshape(B * N, C))
+    ref = torch.cat(parts, dim=-1)
+    err = (dqkv.float() - ref).abs().max().item()
+    assert err <= 2 ** -7 * ref.abs().max().item(), err

@@ -18,6 +18,7 @@ FRSA_FLAG_NO_ROPE = 1
 EXPORTED_SYMBOLS = (
     "frsa_fwd",
     "frsa_qkv_rope",
+    "frsa_qkv_rope_bwd",
     "frsa_bwd",
     "frsa_bwd_workspace_bytes",
     "frsa_strerror",
@@ -85,6 +86,26 @@ class FrsaQkvArgs(ctypes.Structure):
     ]
 
 
+class FrsaQkvBwdArgs(ctypes.Structure):
+    """Mirror of ``frsa_qkv_bwd_args`` (include/frsa.h)."""
+
+    _fields_ = [
+        ("dq", ctypes.c_void_p),
+        ("dk", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p),
+        ("cosp", ctypes.c_void_p),
+        ("sinp", ctypes.c_void_p),
+        ("dqkv", ctypes.c_void_p),
+        ("B", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("n_pos", ctypes.c_int64),
+        ("has_cls", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
 class FrsaError(RuntimeError):
     """A non-zero status returned by the C ABI."""
 
@@ -121,6 +142,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.frsa_query_status.restype = ctypes.c_int
     lib.frsa_qkv_rope.argtypes = [ctypes.POINTER(FrsaQkvArgs), ctypes.c_void_p]
     lib.frsa_qkv_rope.restype = ctypes.c_int
+    lib.frsa_qkv_rope_bwd.argtypes = [ctypes.POINTER(FrsaQkvBwdArgs), ctypes.c_void_p]
+    lib.frsa_qkv_rope_bwd.restype = ctypes.c_int
     lib.frsa_bwd_noalloc.argtypes = [ctypes.POINTER(FrsaAttnArgs), ctypes.c_void_p]
     lib.frsa_bwd_noalloc.restype = ctypes.c_int
     lib.frsa_bwd_noalloc_max_elements.argtypes = []

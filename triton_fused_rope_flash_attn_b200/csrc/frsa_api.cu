@@ -429,6 +429,29 @@ int frsa_qkv_rope(const frsa_qkv_args* a, void* stream) {
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_qkv_rope", e);
 }
 
+int frsa_qkv_rope_bwd(const frsa_qkv_bwd_args* a, void* stream) {
+  if (!a || !a->dq || !a->dk || !a->dv || !a->cosp || !a->sinp || !a->dqkv)
+    return FRSA_ERR_NULL_ARG;
+  if (a->B < 1 || a->N < 1 || a->H < 1 || a->C < 1 || a->C % a->H != 0) return FRSA_ERR_BAD_SHAPE;
+  if (a->has_cls != 0 && a->has_cls != 1) return FRSA_ERR_BAD_SHAPE;
+  if (a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;
+  const long long D = a->C / a->H;
+  if (a->C % 128 != 0 || D % 32 != 0 || D > 128) return FRSA_ERR_UNSUPPORTED_D;
+  if (a->dtype != FRSA_DTYPE_BF16 && a->dtype != FRSA_DTYPE_F16) return FRSA_ERR_UNSUPPORTED_DTYPE;
+  const long long M = a->B * a->N;
+  if (M * (3 * a->C / 8) / 256 > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
+  if (!aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv) || !aligned16(a->dqkv) ||
+      !aligned16(a->cosp) || !aligned16(a->sinp))
+    return FRSA_ERR_MISALIGNED;
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  if (const int rc = pending_error("frsa_qkv_rope_bwd"); rc != FRSA_OK) return rc;
+  const cudaError_t e = frsa::launch_qkv_rope_bwd(
+      a->dtype == FRSA_DTYPE_BF16, a->dq, a->dk, a->dv, a->cosp, a->sinp, a->dqkv, M,
+      static_cast<int>(a->N), static_cast<int>(a->C), static_cast<int>(a->H),
+      static_cast<int>(D), static_cast<int>(a->has_cls), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : launch_error("frsa_qkv_rope_bwd", e);
+}
+
 #ifdef FRSA_TRACE
 // Trace builds only: copy the phase stamps (2048 CTAs x 64 slots) to `host`.
 int frsa_trace_copy(unsigned long long* host, size_t n) {

@@ -50,6 +50,10 @@ cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMa
                             const float* bias, const float* cosp, const float* sinp, void* q,
                             void* k, void* v, long long M, int N, int C, int H, int D,
                             int has_cls, cudaStream_t stream);
+// Its backward epilogue: dq, dk, dv [B, H, N, D] -> dqkv [B*N, 3C], R^T on q, k.
+cudaError_t launch_qkv_rope_bwd(bool bf16, const void* dq, const void* dk, const void* dv,
+                                const float* cosp, const float* sinp, void* dqkv, long long M,
+                                int N, int C, int H, int D, int has_cls, cudaStream_t stream);
 
 // Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
 bool fwd_small_applies(const LaunchShape& s);

@@ -22,6 +22,7 @@
 // divides by 32.
 #include "frsa_internal.h"
 #include "frsa_ptx.cuh"
+#include "frsa_rope.cuh"
 
 namespace frsa {
 
@@ -254,6 +255,84 @@ cudaError_t launch_qkv_rope(bool bf16, const CUtensorMap& tm_x, const CUtensorMa
                 : launch(qkv_rope_kernel<__half, 256>, sizeof(QkvSmem<256>) + 1024);
   return bf16 ? launch(qkv_rope_kernel<__nv_bfloat16, 128>, sizeof(QkvSmem<128>) + 1024)
               : launch(qkv_rope_kernel<__half, 128>, sizeof(QkvSmem<128>) + 1024);
+}
+
+namespace {
+
+// Backward of the projection's epilogue: the gradients of q, k, v
+// ([B, H, N, D] each, with respect to the rotated q and k) become the
+// gradient of the projection output, dqkv [B*N, 3C] (the layout the two
+// GEMMs dx = dqkv W and dW = dqkv^T x read), with R^T applied to the q and k
+// parts in f32 and one rounding. One thread per 8-element granule of a dqkv
+// row: the stores are coalesced, the loads read 16 bytes of one head row.
+struct QkvBwdParams {
+  const void* dq;
+  const void* dk;
+  const void* dv;
+  const float* cosp;
+  const float* sinp;
+  void* dqkv;
+  long long M;   // B * N
+  int N, C, H, D, has_cls;
+};
+
+template <typename T>
+__global__ void qkv_rope_bwd_kernel(const QkvBwdParams p) {
+  const int G = 3 * p.C / 8;   // granules of a dqkv row
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long m = idx / G;
+  if (m >= p.M) return;
+  const int f = 8 * static_cast<int>(idx - m * G);
+  const int part = f / p.C, fc = f - part * p.C;
+  const int h = fc / p.D, d0 = fc - h * p.D;
+  const long long b = m / p.N;
+  const int n = static_cast<int>(m - b * p.N);
+  const void* g = part == 0 ? p.dq : (part == 1 ? p.dk : p.dv);
+  const uint4 x = __ldg(reinterpret_cast<const uint4*>(
+      static_cast<const T*>(g) + ((b * p.H + h) * p.N + n) * p.D + d0));
+  float v[8];
+  const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = Elt<T>::unpack(w[e]);
+    v[2 * e] = t.x;
+    v[2 * e + 1] = t.y;
+  }
+  const int pos = part < 2 ? rope_pos(n, p.N, p.has_cls) : -1;
+  if (pos >= 0) {
+    const size_t t0 = static_cast<size_t>(pos) * (p.D >> 1) + (d0 >> 1);
+    unrotate8(v, __ldg(reinterpret_cast<const float4*>(p.cosp + t0)),
+              __ldg(reinterpret_cast<const float4*>(p.sinp + t0)));
+  }
+  reinterpret_cast<uint4*>(static_cast<T*>(p.dqkv) + m * 3 * p.C + f)[0] = pack8<T>(v);
+}
+
+}  // namespace
+
+cudaError_t launch_qkv_rope_bwd(bool bf16, const void* dq, const void* dk, const void* dv,
+                                const float* cosp, const float* sinp, void* dqkv, long long M,
+                                int N, int C, int H, int D, int has_cls, cudaStream_t stream) {
+  QkvBwdParams p;
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.cosp = cosp;
+  p.sinp = sinp;
+  p.dqkv = dqkv;
+  p.M = M;
+  p.N = N;
+  p.C = C;
+  p.H = H;
+  p.D = D;
+  p.has_cls = has_cls;
+  const long long threads = M * (3LL * C / 8);
+  if (threads == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  if (bf16)
+    qkv_rope_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(p);
+  else
+    qkv_rope_bwd_kernel<__half><<<blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace frsa

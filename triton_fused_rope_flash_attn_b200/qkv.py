@@ -7,8 +7,9 @@ attention block does before the attention (reference README:156-159: timm's
 rotates q and k by token position and writes q, k, v as ``[B, H, N, D]``.
 The attention over these q, k then runs with ``rope=False`` (the C ABI's
 FRSA_FLAG_NO_ROPE: the kernels rotate nothing), so the rotation leaves the
-attention kernels. The backward applies ``R^T`` to dq and dk and uses torch
-GEMMs for dx, dW and db.
+attention kernels. The backward is one kernel (``frsa_qkv_rope_bwd``) that
+applies ``R^T`` to dq and dk and merges the heads back into the projection
+output's gradient ``[B*N, 3C]``, then two GEMMs for dx and dW.
 """
 from __future__ import annotations
 
@@ -22,21 +23,6 @@ def supported(C: int, num_heads: int, dtype: torch.dtype) -> bool:
     D = C // num_heads
     return (C % num_heads == 0 and C % 128 == 0 and D % 32 == 0 and D <= 128
             and dtype in (torch.bfloat16, torch.float16))
-
-
-def _rot_tables(cosp, sinp, N, has_cls, dtype):
-    """Per-token (cos, sin) ``[N, D/2]`` with identity rows for CLS."""
-    off = 1 if has_cls else 0
-    C = torch.ones(N, cosp.shape[1], device=cosp.device, dtype=dtype)
-    S = torch.zeros(N, cosp.shape[1], device=cosp.device, dtype=dtype)
-    C[off:], S[off:] = cosp[: N - off], sinp[: N - off]
-    return C, S
-
-
-def _unrotate(g, C, S):
-    """R^T applied to pairs of the last dim of ``g`` [B, H, N, D]."""
-    e, o = g[..., 0::2], g[..., 1::2]
-    return torch.stack((e * C + o * S, o * C - e * S), dim=-1).flatten(-2)
 
 
 class QKVRope(torch.autograd.Function):
@@ -65,21 +51,31 @@ class QKVRope(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
+        # One kernel (frsa_qkv_rope_bwd) turns dq, dk, dv into the gradient of
+        # the projection output, dqkv [B*N, 3C] (R^T on the q and k parts);
+        # the weight and input gradients are then two plain GEMMs.
         x, w, cosp, sinp = ctx.saved_tensors
         num_heads, has_cls = ctx.meta
         B, N, C = x.shape
-        Ct, St = _rot_tables(cosp, sinp, N, has_cls, torch.float32)
-        parts = []
-        for g, rot in ((dq, True), (dk, True), (dv, False)):
-            g = torch.zeros(B, num_heads, N, C // num_heads, device=x.device) if g is None \
-                else g.float()
-            if rot:
-                g = _unrotate(g, Ct, St)
-            parts.append(g.transpose(1, 2).reshape(B, N, C))
-        dqkv = torch.cat(parts, dim=-1).to(x.dtype)            # [B, N, 3C]
-        dx = dqkv @ w                                          # [B, N, C]
-        dw = dqkv.reshape(-1, 3 * C).t() @ x.reshape(-1, C)    # [3C, C]
-        db = dqkv.float().sum(dim=(0, 1)) if ctx.has_bias else None
+        D = C // num_heads
+        grads = []
+        for g in (dq, dk, dv):
+            g = torch.zeros(B, num_heads, N, D, device=x.device, dtype=x.dtype) if g is None \
+                else g.to(x.dtype).contiguous()
+            grads.append(g)
+        dqkv = torch.empty(B * N, 3 * C, device=x.device, dtype=x.dtype)
+        a = _lib.FrsaQkvBwdArgs()
+        a.dq, a.dk, a.dv = (g.data_ptr() for g in grads)
+        a.cosp, a.sinp = cosp.data_ptr(), sinp.data_ptr()
+        a.dqkv = dqkv.data_ptr()
+        a.B, a.N, a.C, a.H, a.n_pos = B, N, C, num_heads, cosp.shape[0]
+        a.has_cls = int(bool(has_cls))
+        a.dtype = _lib.FRSA_DTYPE_BF16 if x.dtype == torch.bfloat16 else _lib.FRSA_DTYPE_F16
+        _lib.check(_lib.load().frsa_qkv_rope_bwd(
+            a, torch.cuda.current_stream(x.device).cuda_stream), "frsa_qkv_rope_bwd")
+        dx = (dqkv @ w).view(B, N, C)                          # [B, N, C]
+        dw = dqkv.t() @ x.reshape(-1, C)                       # [3C, C]
+        db = dqkv.float().sum(dim=0) if ctx.has_bias else None
         return dx, dw, db, None, None, None, None
 
 
