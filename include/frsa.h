@@ -210,6 +210,33 @@ typedef struct frsa_qkv_bwd_args {
 
 int frsa_qkv_rope_bwd(const frsa_qkv_bwd_args* args, void* stream);
 
+/* f32 inputs under 16-bit compute (the reference converts f32 loads to the
+ * compute type, fa_rope_full .py:168-174, 240-246). frsa_convert_in reads q,
+ * k, v (f32, contiguous [B, H, N, D]) and writes q_out = R(q), k_out = R(k)
+ * and v_out in `dtype` (BF16 or F16), rotated in f32 and rounded once, so
+ * that frsa_fwd / frsa_bwd then run with FRSA_FLAG_NO_ROPE. frsa_convert_out
+ * is its backward: q, k, v are the 16-bit gradients with respect to q_out,
+ * k_out, v_out, and q_out, k_out, v_out receive dq = R^T dq^, dk = R^T dk^
+ * and dv in f32. Rotation as in frsa_fwd (table row n - has_cls, the CLS
+ * token untouched). D % 8 == 0, every pointer 16-byte aligned. No direct
+ * counterpart in the reference (its kernels convert while loading). */
+typedef struct frsa_convert_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  const float* cosp;
+  const float* sinp;
+  int64_t B, H, N, D, n_pos;
+  int32_t has_cls;
+  int32_t dtype;      /* enum frsa_dtype of the 16-bit side: BF16 or F16 */
+} frsa_convert_args;
+
+int frsa_convert_in(const frsa_convert_args* args, void* stream);
+int frsa_convert_out(const frsa_convert_args* args, void* stream);
+
 /* FRSA_ABI_VERSION of the loaded library. */
 int frsa_abi_version(void);
 

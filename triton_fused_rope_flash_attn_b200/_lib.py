@@ -19,6 +19,8 @@ EXPORTED_SYMBOLS = (
     "frsa_fwd",
     "frsa_qkv_rope",
     "frsa_qkv_rope_bwd",
+    "frsa_convert_in",
+    "frsa_convert_out",
     "frsa_bwd",
     "frsa_bwd_workspace_bytes",
     "frsa_strerror",
@@ -106,6 +108,28 @@ class FrsaQkvBwdArgs(ctypes.Structure):
     ]
 
 
+class FrsaConvertArgs(ctypes.Structure):
+    """Mirror of ``frsa_convert_args`` (include/frsa.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p),
+        ("k_out", ctypes.c_void_p),
+        ("v_out", ctypes.c_void_p),
+        ("cosp", ctypes.c_void_p),
+        ("sinp", ctypes.c_void_p),
+        ("B", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("D", ctypes.c_int64),
+        ("n_pos", ctypes.c_int64),
+        ("has_cls", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
 class FrsaError(RuntimeError):
     """A non-zero status returned by the C ABI."""
 
@@ -144,6 +168,9 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.frsa_qkv_rope.restype = ctypes.c_int
     lib.frsa_qkv_rope_bwd.argtypes = [ctypes.POINTER(FrsaQkvBwdArgs), ctypes.c_void_p]
     lib.frsa_qkv_rope_bwd.restype = ctypes.c_int
+    for name in ("frsa_convert_in", "frsa_convert_out"):
+        getattr(lib, name).argtypes = [ctypes.POINTER(FrsaConvertArgs), ctypes.c_void_p]
+        getattr(lib, name).restype = ctypes.c_int
     lib.frsa_bwd_noalloc.argtypes = [ctypes.POINTER(FrsaAttnArgs), ctypes.c_void_p]
     lib.frsa_bwd_noalloc.restype = ctypes.c_int
     lib.frsa_bwd_noalloc_max_elements.argtypes = []

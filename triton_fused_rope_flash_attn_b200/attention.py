@@ -178,6 +178,23 @@ def _fp32_backward(Q, K, V, O, lse, dO, COSP, SINP, has_cls, rope=True):
     return dq, dk, dv
 
 
+def _convert(to_16bit, srcs, dsts, COSP, SINP, has_cls, comp):
+    """frsa_convert_in (f32 q, k, v -> rotated 16-bit) or frsa_convert_out
+    (16-bit dq^, dk^, dv -> f32 with R^T) on torch's current stream."""
+    B, H, N, D = srcs[0].shape
+    a = _lib.FrsaConvertArgs()
+    a.q, a.k, a.v = (t.data_ptr() for t in srcs)
+    a.q_out, a.k_out, a.v_out = (t.data_ptr() for t in dsts)
+    a.cosp, a.sinp = COSP.data_ptr(), SINP.data_ptr()
+    a.B, a.H, a.N, a.D, a.n_pos = B, H, N, D, COSP.shape[0]
+    a.has_cls = int(bool(has_cls))
+    a.dtype = _DT_CODE[comp]
+    lib = _lib.load()
+    fn = lib.frsa_convert_in if to_16bit else lib.frsa_convert_out
+    _lib.check(fn(a, torch.cuda.current_stream(srcs[0].device).cuda_stream),
+               "frsa_convert_in" if to_16bit else "frsa_convert_out")
+
+
 class TritonAttention(torch.autograd.Function):
     """Fused 2D-RoPE SDPA with the reference's autograd contract (fa_rope_full .py:1011-1138)."""
 
@@ -204,10 +221,23 @@ class TritonAttention(torch.autograd.Function):
         ctx.has_cls = has_cls
         ctx.rope = rope
         ctx.io_dtypes = (Q.dtype, K.dtype, V.dtype)
+        ctx.convert = False
         if comp == torch.float32:
             Qf, Kf, Vf = (t.float().contiguous() for t in (Q, K, V))
             o, lse = _fp32_forward(Qf, Kf, Vf, COSP, SINP, has_cls, rope)
             ctx.save_for_backward(Qf, Kf, Vf, o, lse, COSP, SINP)
+            return o.to(Q.dtype)
+        ctx.convert = (rope and Q.dtype == K.dtype == V.dtype == torch.float32
+                       and HEAD_DIM % 8 == 0)
+        if ctx.convert:
+            # f32 inputs, 16-bit compute: one kernel converts q, k, v and
+            # applies the rotation (in f32, one rounding); the attention then
+            # rotates nothing, and the backward converts the gradients back.
+            Qf, Kf, Vf = (t.contiguous() for t in (Q, K, V))
+            qc, kc, vc = (torch.empty(Q.shape, device=Q.device, dtype=comp) for _ in range(3))
+            _convert(True, (Qf, Kf, Vf), (qc, kc, vc), COSP, SINP, has_cls, comp)
+            o, lse = fused_rope_attention_fwd(qc, kc, vc, None, None, has_cls, rope=False)
+            ctx.save_for_backward(qc, kc, vc, o, lse, COSP, SINP)
             return o.to(Q.dtype)
         qc, kc, vc = (t.to(comp) for t in (Q, K, V))
         o, lse = fused_rope_attention_fwd(qc, kc, vc, COSP, SINP, has_cls, rope=rope)
@@ -220,6 +250,12 @@ class TritonAttention(torch.autograd.Function):
         if ctx.comp == torch.float32:
             dq, dk, dv = _fp32_backward(qc, kc, vc, o, lse, dO.float(), COSP, SINP, ctx.has_cls,
                                         ctx.rope)
+        elif ctx.convert:
+            gq, gk, gv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), None, None,
+                                                  ctx.has_cls, rope=False)
+            dq, dk, dv = (torch.empty(qc.shape, device=qc.device, dtype=torch.float32)
+                          for _ in range(3))
+            _convert(False, (gq, gk, gv), (dq, dk, dv), COSP, SINP, ctx.has_cls, ctx.comp)
         else:
             dq, dk, dv = fused_rope_attention_bwd(qc, kc, vc, o, lse, dO.to(ctx.comp), COSP, SINP,
                                                   ctx.has_cls, rope=ctx.rope)

@@ -18,6 +18,7 @@
 #include "frsa_fwd_small.cu"
 #include "frsa_tf32.cu"
 #include "frsa_qkv.cu"
+#include "frsa_convert.cu"
 
 namespace frsa {
 
@@ -450,6 +451,38 @@ int frsa_qkv_rope_bwd(const frsa_qkv_bwd_args* a, void* stream) {
       static_cast<int>(a->N), static_cast<int>(a->C), static_cast<int>(a->H),
       static_cast<int>(D), static_cast<int>(a->has_cls), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FRSA_OK : launch_error("frsa_qkv_rope_bwd", e);
+}
+
+static int convert_common(const frsa_convert_args* a, bool in, const char* where, void* stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->q_out || !a->k_out || !a->v_out || !a->cosp ||
+      !a->sinp)
+    return FRSA_ERR_NULL_ARG;
+  if (a->B < 1 || a->H < 1 || a->N < 1 || a->D < 8) return FRSA_ERR_BAD_SHAPE;
+  if (a->has_cls != 0 && a->has_cls != 1) return FRSA_ERR_BAD_SHAPE;
+  if (a->N - a->has_cls > a->n_pos) return FRSA_ERR_BAD_SHAPE;
+  if (a->D % 8 != 0 || a->D > 128) return FRSA_ERR_UNSUPPORTED_D;
+  if (a->dtype != FRSA_DTYPE_BF16 && a->dtype != FRSA_DTYPE_F16) return FRSA_ERR_UNSUPPORTED_DTYPE;
+  const long long rows = a->B * a->H * a->N;
+  if (rows * (a->D / 8) / 256 > 0x7FFFFFFFLL || a->N > (1LL << 30)) return FRSA_ERR_BAD_SHAPE;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->q_out) ||
+      !aligned16(a->k_out) || !aligned16(a->v_out) || !aligned16(a->cosp) || !aligned16(a->sinp))
+    return FRSA_ERR_MISALIGNED;
+  if (!device_is_sm100()) return FRSA_ERR_NO_DEVICE;
+  if (const int rc = pending_error(where); rc != FRSA_OK) return rc;
+  const void* src[3] = {a->q, a->k, a->v};
+  void* dst[3] = {a->q_out, a->k_out, a->v_out};
+  const cudaError_t e = frsa::launch_convert(
+      in, a->dtype == FRSA_DTYPE_BF16, src, dst, a->cosp, a->sinp, rows, static_cast<int>(a->N),
+      static_cast<int>(a->D), static_cast<int>(a->has_cls), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FRSA_OK : launch_error(where, e);
+}
+
+int frsa_convert_in(const frsa_convert_args* a, void* stream) {
+  return convert_common(a, true, "frsa_convert_in", stream);
+}
+
+int frsa_convert_out(const frsa_convert_args* a, void* stream) {
+  return convert_common(a, false, "frsa_convert_out", stream);
 }
 
 #ifdef FRSA_TRACE

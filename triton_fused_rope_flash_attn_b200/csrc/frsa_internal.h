@@ -55,6 +55,12 @@ cudaError_t launch_qkv_rope_bwd(bool bf16, const void* dq, const void* dk, const
                                 const float* cosp, const float* sinp, void* dqkv, long long M,
                                 int N, int C, int H, int D, int has_cls, cudaStream_t stream);
 
+// f32 <-> 16-bit conversion with the rotation (frsa_convert.cu): in: q, k, v
+// f32 -> R(q), R(k), v 16-bit; out: 16-bit dq^, dk^, dv -> R^T dq^, R^T dk^, dv f32.
+cudaError_t launch_convert(bool in, bool bf16, const void* const* src, void* const* dst,
+                           const float* cosp, const float* sinp, long long rows, int N, int D,
+                           int has_cls, cudaStream_t stream);
+
 // Persistent forward for N <= 256, D <= 64 (RoPE tables resident in shared memory).
 bool fwd_small_applies(const LaunchShape& s);
 cudaError_t launch_fwd_small(const LaunchShape& s, const CUtensorMap& tm_q,

@@ -83,10 +83,11 @@ def sdpa_fa_rope_op(Q: Tensor, K: Tensor, V: Tensor, cos_sin, *, has_cls: bool =
     D = Q.shape[-1]
     assert (D % 4) == 0, "HEAD_DIM must be divisible by 4 (2D RoPE requires pairs)."
     comp = _sdpa_comp_dtype(Q)
-    if comp == torch.float32:
+    if comp == torch.float32 or Q.dtype == torch.float32:
         # float32 compute picks per-call power-of-two range factors from the
-        # data, which a traced graph cannot hold: it runs through the
-        # autograd.Function path (eager).
+        # data, which a traced graph cannot hold, and float32 inputs under
+        # 16-bit autocast go through the fused conversion kernels: both run
+        # through the autograd.Function path (eager).
         return TritonAttention.apply(Q, K, V, cos_sin, math.isqrt(cos_sin.tables()[0].shape[0]),
                                      has_cls)
     COSP, SINP = cos_sin.tables()
