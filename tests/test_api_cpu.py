@@ -192,3 +192,44 @@ def test_strides_and_flags_validated(lib):
     rope = _args(n_pos=0)
     rope.cosp = rope.sinp = None
     assert code(rope) == 1                                  # tables needed
+
+
+def test_convert_and_qkv_bwd_validation(lib):
+    """frsa_convert_in/out and frsa_qkv_rope_bwd reject bad arguments before
+    touching a device (codes from include/frsa.h)."""
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.addressof(buf) + (-ctypes.addressof(buf)) % 256   # 256-byte aligned host stand-in
+
+    def conv(**kw):
+        a = _lib.FrsaConvertArgs()
+        a.q = a.k = a.v = a.q_out = a.k_out = a.v_out = a.cosp = a.sinp = p
+        a.B, a.H, a.N, a.D, a.n_pos, a.has_cls = 1, 2, 197, 64, 196, 1
+        a.dtype = _lib.FRSA_DTYPE_BF16
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    for fn in (lib.frsa_convert_in, lib.frsa_convert_out):
+        assert fn(None, None) == 1                        # NULL_ARG
+        assert fn(ctypes.byref(conv(q=None)), None) == 1
+        assert fn(ctypes.byref(conv(N=0)), None) == 2     # BAD_SHAPE
+        assert fn(ctypes.byref(conv(n_pos=100)), None) == 2   # table shorter than the tokens
+        assert fn(ctypes.byref(conv(D=36)), None) == 3    # UNSUPPORTED_D
+        assert fn(ctypes.byref(conv(dtype=_lib.FRSA_DTYPE_F32)), None) == 4
+        assert fn(ctypes.byref(conv(q=p + 8)), None) == 5     # MISALIGNED
+
+    def qb(**kw):
+        a = _lib.FrsaQkvBwdArgs()
+        a.dq = a.dk = a.dv = a.cosp = a.sinp = a.dqkv = p
+        a.B, a.N, a.C, a.H, a.n_pos, a.has_cls = 1, 197, 768, 12, 196, 1
+        a.dtype = _lib.FRSA_DTYPE_BF16
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    assert lib.frsa_qkv_rope_bwd(None, None) == 1
+    assert lib.frsa_qkv_rope_bwd(ctypes.byref(qb(dqkv=None)), None) == 1
+    assert lib.frsa_qkv_rope_bwd(ctypes.byref(qb(C=770)), None) == 2     # C % H != 0
+    assert lib.frsa_qkv_rope_bwd(ctypes.byref(qb(C=384, H=16)), None) == 3   # D = 24
+    assert lib.frsa_qkv_rope_bwd(ctypes.byref(qb(dtype=_lib.FRSA_DTYPE_F32)), None) == 4
+    assert lib.frsa_qkv_rope_bwd(ctypes.byref(qb(dq=p + 4)), None) == 5
